@@ -1,0 +1,395 @@
+"""Benchmark: SSIM + gradient throughput (Gpixel/s, % of HBM roofline) at 1/2/4/8 B200s,
+plus the full-HD SSIM latency.
+
+Workload (one step): 2048 images x 3 x 512 x 512 Float32 (x ~ U[0,1),
+y = clamp(x + N(0, 0.1^2), 0, 1)), SSIM values and dSSIM/dx for every image;
+the batch is split evenly over the N ranks (strong scaling, one process per
+GPU) and the 2048 per-image SSIMs are all-gathered over NCCL.  Inputs are
+12.9 GB, far larger than L2, so no flush is needed between steps.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+For N > 1 launch with torch.distributed.run (one rank per GPU).  Rank 0 prints
+one JSON line.  ``--impl reference`` times the reference algorithm's CPU
+restatement (the oracle; FastCUDASSIM.jl itself needs Julia, which is absent)
+on the host cores, on a bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+N_IMAGES, C, H, W = 2048, 3, 512, 512
+NOISE = 0.1
+BYTES_PER_ELEM = 4 + 4 + 4      # x, y read; gradient written (Float32)
+WORKLOAD = "ssim_with_gradient 2048x3x512x512 f32, batch-sharded, NCCL all-gather of per-image SSIM"
+
+
+def measured_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            d = json.load(f)
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def traffic_per_launch(n_local):
+    """DRAM bytes per launch from the committed ncu summary (bytes per element x elements), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "traffic.json")) as f:
+            d = json.load(f)
+        return float(d["dram_bytes_per_elem"]) * n_local * C * H * W
+    except Exception:
+        return None
+
+
+class ClockSampler:
+    """nvidia-smi clocks and throttle reasons sampled every 200 ms during the timed region."""
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index):
+        self.index = index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        sms, maxes, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            p = [s.strip() for s in ln.split(",")]
+            if len(p) < 9:
+                continue
+            try:
+                sms.append(float(p[1]))
+                maxes.append(float(p[2]))
+            except ValueError:
+                continue
+            for nm, v in zip(names, p[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sms) if sms else None, "sm_max_mhz": max(maxes) if maxes else None,
+                "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def cpu_oracle_rate(n_images, nthreads, reps=1):
+    """Gpixel/s of the oracle (reference algorithm, single precision) on host cores."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    import __graft_entry__ as ge
+    syn = __import__(ge.load_package().__name__ + ".synthetic", fromlist=["x"])
+    x, y = syn.host_pair(99, (C, H, W, n_images), NOISE)
+    oracle.ssim(x[..., :1], y[..., :1], nthreads=nthreads)   # warm the library
+    best = None
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        oracle.ssim(x, y, nthreads=nthreads)
+        dt = time.perf_counter() - t0
+        best = dt if best is None else min(best, dt)
+    return n_images * H * W / best / 1e9, best
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return 0
+    threads = os.cpu_count() or 1
+    sample = 4
+    for _ in range(args.warmup):
+        cpu_oracle_rate(sample, threads)
+    times = []
+    for _ in range(args.steps):
+        _, dt = cpu_oracle_rate(sample, threads)
+        times.append(dt)
+    t = sum(times)
+    value = args.steps * sample * H * W / t / 1e9
+    line = {
+        "impl": "reference", "metric": "SSIM+grad Gpixel/s", "value": value, "unit": "Gpixel/s",
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * t / args.steps, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": WORKLOAD, "sample_images_per_step": sample},
+        "cpu_baseline": {"value": value, "unit": "Gpixel/s", "cores": threads, "kind": "port",
+                         "sample": f"{sample} images of 3x512x512 with gradient per step (the oracle: "
+                                   "FastCUDASSIM.jl's algorithm restated in C; Julia is not available)"},
+        "e2e": {"value": value, "unit": "Gpixel/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    syn = __import__(pkg.__name__ + ".synthetic", fromlist=["x"])
+    sharded = __import__(pkg.__name__ + ".sharded", fromlist=["x"])
+    nat = pkg._native
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    lo, hi = sharded.shard_range(N_IMAGES, world, rank)
+    n_local = hi - lo
+    x, y = syn.device_pair((C, H, W, n_local), NOISE, seed=1000 + rank, device=dev)
+    grad = pkg.jl_empty((C, H, W, n_local), torch.float32, dev)
+    ssims = torch.empty(n_local, dtype=torch.float32, device=dev)
+    all_scores = torch.empty(N_IMAGES, dtype=torch.float32, device=dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        pkg.ssim_with_gradient_(ssims, grad, x, y, None, True)
+        if world > 1:
+            all_scores.copy_(sharded.gather_scores(ssims, N_IMAGES))
+        else:
+            all_scores.copy_(ssims)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(args.warmup):
+        step()
+    barrier()
+    sampler = ClockSampler(local)
+    sampler.start()
+    k0 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    k1 = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    e0.record(stream)
+    for i in range(args.steps):
+        k0[i].record(stream)
+        pkg.ssim_with_gradient_(ssims, grad, x, y, None, True)
+        k1[i].record(stream)
+        if world > 1:
+            all_scores.copy_(sharded.gather_scores(ssims, N_IMAGES))
+        else:
+            all_scores.copy_(ssims)
+    e1.record(stream)
+    barrier()
+    clocks = sampler.stop()
+    elapsed = e0.elapsed_time(e1) / 1e3
+    kern = sum(a.elapsed_time(b) for a, b in zip(k0, k1)) / 1e3 / args.steps
+    t = torch.tensor([elapsed, kern], dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed, kern = float(t[0]), float(t[1])
+
+    # ---- end to end: host buffers through the public API, copies inside the timed region
+    e2e = None
+    if not args.no_e2e:
+        hx = torch.empty(x.numel(), dtype=torch.float32, pin_memory=True)
+        hy = torch.empty(y.numel(), dtype=torch.float32, pin_memory=True)
+        hx.copy_(x.permute(3, 2, 1, 0).reshape(-1))
+        hy.copy_(y.permute(3, 2, 1, 0).reshape(-1))
+        hs = torch.empty(N_IMAGES, dtype=torch.float32, pin_memory=True)
+        dx = pkg.jl_empty((C, H, W, n_local), torch.float32, dev)
+        dy = pkg.jl_empty((C, H, W, n_local), torch.float32, dev)
+        dxf = dx.permute(3, 2, 1, 0).reshape(-1)
+        dyf = dy.permute(3, 2, 1, 0).reshape(-1)
+        e2e_steps = max(1, min(args.steps, 3))
+
+        def e2e_step():
+            dxf.copy_(hx, non_blocking=True)
+            dyf.copy_(hy, non_blocking=True)
+            pkg.ssim_with_gradient_(ssims, grad, dx, dy, None, True)
+            scores = sharded.gather_scores(ssims, N_IMAGES) if world > 1 else ssims
+            hs.copy_(scores, non_blocking=True)
+
+        e2e_step()
+        barrier()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        b.record(stream)
+        barrier()
+        te = torch.tensor([a.elapsed_time(b) / 1e3], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(te, op=dist.ReduceOp.MAX)
+        e2e = {"value": e2e_steps * N_IMAGES * H * W / float(te[0]) / 1e9, "unit": "Gpixel/s",
+               "h2d_bytes_per_step": int(2 * n_local * C * H * W * 4), "d2h_bytes_per_step": int(N_IMAGES * 4),
+               "steps": e2e_steps}
+        del hx, hy, dx, dy, dxf, dyf
+
+    extras = {}
+    if rank == 0 and not args.no_extras:
+        extras = side_benchmarks(pkg, dev)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        n_cpu = 16
+        rate, dt = cpu_oracle_rate(n_cpu, os.cpu_count() or 1)
+        cpu = {"value": rate, "unit": "Gpixel/s", "cores": os.cpu_count() or 1, "kind": "port",
+               "sample": f"{n_cpu} images of 3x512x512 with gradient ({dt:.1f} s), oracle in C with pthreads"}
+
+    if world > 1:
+        dist.barrier(device_ids=[local])
+        dist.destroy_process_group()
+    if rank != 0:
+        return 0
+    peak, peak_kind = measured_peaks()
+    pixels = N_IMAGES * H * W
+    value = args.steps * pixels / elapsed / 1e9
+    alg_bytes = n_local * C * H * W * BYTES_PER_ELEM
+    achieved = alg_bytes / kern / 1e9
+    line = {
+        "metric": "SSIM+grad Gpixel/s", "value": value, "unit": "Gpixel/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * elapsed / args.steps,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (device RNG, seeded)",
+        "config": {"workload": WORKLOAD, "images": N_IMAGES, "images_per_gpu": n_local, "shape": [C, H, W],
+                   "noise_sigma": NOISE, "l2": "inputs (12.9 GB) larger than L2, no flush",
+                   "parallelism": f"batch-shard x{world}"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
+                     "traffic": traffic_per_launch(n_local),
+                     "kernel": "fssim::band_kernel<96,true,true>", "kernel_ms": kern * 1e3,
+                     "alg_bytes_per_launch": alg_bytes},
+        "cpu_baseline": cpu,
+        "e2e": e2e,
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+        "gelem_per_s": value * C,
+    }
+    line.update(extras)
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def side_benchmarks(pkg, dev):
+    """Full-HD SSIM latency (3x1080x1920 forward) and the 32x3x256x256 DSSIM + gradient call,
+    each timed with CUDA events after an L2 flush (their inputs fit in L2)."""
+    import torch
+    syn = __import__(pkg.__name__ + ".synthetic", fromlist=["x"])
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    out = {}
+
+    def timed(fn, reps=30):
+        ts = []
+        for i in range(reps + 3):
+            flush.zero_()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            b.synchronize()
+            if i >= 3:
+                ts.append(a.elapsed_time(b))
+        return statistics.median(ts)
+
+    for name, shape, noise in (("fullhd_1ch", (1, 1080, 1920), 0.1), ("fullhd_3ch", (3, 1080, 1920), 0.05)):
+        x, y = syn.device_pair(shape, noise, device=dev)
+        s = torch.empty(1, dtype=torch.float32, device=dev)
+        ms = timed(lambda: pkg.ssim_(s, x, y))
+        walls = []
+        for _ in range(20):
+            flush.zero_()
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            pkg.ssim(x, y)                      # returns a Python float: includes the D2H read
+            walls.append((time.perf_counter() - t0) * 1e3)
+        nbytes = x.numel() * 8
+        out[f"{name}_ssim_ms"] = ms
+        out[f"{name}_ssim_api_wall_ms"] = statistics.median(walls)
+        out[f"{name}_ssim_hbm_frac"] = nbytes / (ms / 1e3) / 1e9 / measured_peaks()[0]
+    x, y = syn.device_pair((3, 256, 256, 32), None, device=dev)
+    d = torch.empty(32, dtype=torch.float32, device=dev)
+    g = pkg.jl_empty((3, 256, 256, 32), torch.float32, dev)
+    ms = timed(lambda: pkg.dssim_with_gradient_(d, g, x, y, None, True))
+    out["batch32_3x256x256_dssim_grad_ms"] = ms
+    out["batch32_3x256x256_dssim_grad_hbm_frac"] = x.numel() * 12 / (ms / 1e3) / 1e9 / measured_peaks()[0]
+    return out
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu", action="store_true")
+    ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--profile-case", choices=["fused", "fwd"], default=None,
+                    help="only run the kernel on 64x3x512x512 f32 (a size for ncu captures): "
+                         "warmup + steps launches, no timing output")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.profile_case:
+        return profile_case(args)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+def profile_case(args):
+    """warmup + steps launches of one kernel on 64x3x512x512 f32 (0.3 GB, larger than L2)."""
+    import torch
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    syn = __import__(pkg.__name__ + ".synthetic", fromlist=["x"])
+    shape = (C, H, W, 64)
+    x, y = syn.device_pair(shape, NOISE)
+    s = torch.empty(64, dtype=torch.float32, device="cuda")
+    g = pkg.jl_empty(shape, torch.float32)
+    for _ in range(args.warmup + args.steps):
+        if args.profile_case == "fused":
+            pkg.ssim_with_gradient_(s, g, x, y, None, True)
+        else:
+            pkg.ssim_(s, x, y)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": args.profile_case, "launches": args.warmup + args.steps,
+                      "ssim0": float(s[0])}))
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())

@@ -1,0 +1,103 @@
+"""ctypes binding of ``libfastssim.so`` (C ABI declared in ``include/fastssim.h``).
+
+The library is built in-tree by ``build.py`` into ``lib/libfastssim.so``.  There
+is no fallback: if the library is missing or cannot be loaded, every call raises.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_HERE, "lib", "libfastssim.so")
+
+# enum fssim_dtype
+FLOAT32, FLOAT16, N0F8, FLOAT64 = 0, 1, 2, 3
+# enum fssim_flags
+SKIP_SSIM = 1 << 0
+SKIP_BACKWARD = 1 << 1
+USE_DSSIM = 1 << 2
+DIVIDE_BY_TWO = 1 << 3
+SHOULD_ZERO = 1 << 4
+# enum fssim_status
+OK = 0
+ERR_INVALID_ARGUMENT = 1
+ERR_DIMENSION_MISMATCH = 2
+ERR_UNSUPPORTED_DTYPE = 3
+ERR_WORKSPACE = 4
+ERR_MISALIGNED = 5
+ERR_CUDA = 6
+
+EXPORTED_SYMBOLS = ("fssim_version", "fssim_last_error", "fssim_workspace_size", "fssim_fwd_bwd")
+
+
+class FastSSIMError(RuntimeError):
+    """A nonzero status returned by the native library."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"[fastssim status {status}] {message}")
+        self.status = status
+
+
+class DimensionMismatch(ValueError):
+    """Mirror of Julia's ``DimensionMismatch`` thrown by the reference's driver."""
+
+
+_lib = None
+
+
+def load() -> ctypes.CDLL:
+    """Load the native library (once).  Raises if it has not been built."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not os.path.exists(LIB_PATH):
+        raise FastSSIMError(ERR_CUDA, f"native library not built: {LIB_PATH} is missing "
+                                      "(run __graft_entry__.build() or fastcudassim build.py)")
+    lib = ctypes.CDLL(LIB_PATH)
+    i64, u32, vp, sz = ctypes.c_int64, ctypes.c_uint32, ctypes.c_void_p, ctypes.c_size_t
+    lib.fssim_version.argtypes = []
+    lib.fssim_version.restype = ctypes.c_char_p
+    lib.fssim_last_error.argtypes = [ctypes.c_char_p, sz]
+    lib.fssim_last_error.restype = ctypes.c_int
+    lib.fssim_workspace_size.argtypes = [i64, i64, i64, i64, u32, ctypes.POINTER(sz)]
+    lib.fssim_workspace_size.restype = ctypes.c_int
+    lib.fssim_fwd_bwd.argtypes = [vp, ctypes.c_int, i64, vp, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int,
+                                  vp, i64, i64, i64, i64, u32, vp, sz, vp]
+    lib.fssim_fwd_bwd.restype = ctypes.c_int
+    _lib = lib
+    return lib
+
+
+def last_error() -> tuple[int, str]:
+    buf = ctypes.create_string_buffer(512)
+    st = load().fssim_last_error(buf, len(buf))
+    return st, buf.value.decode(errors="replace")
+
+
+def check(status: int) -> None:
+    """Raise the Python exception that matches a nonzero status."""
+    if status == OK:
+        return
+    _, msg = last_error()
+    if status == ERR_DIMENSION_MISMATCH:
+        raise DimensionMismatch(msg)
+    raise FastSSIMError(status, msg)
+
+
+def version() -> str:
+    return load().fssim_version().decode()
+
+
+def workspace_size(c: int, h: int, w: int, n: int, flags: int) -> int:
+    out = ctypes.c_size_t(0)
+    check(load().fssim_workspace_size(c, h, w, n, flags, ctypes.byref(out)))
+    return int(out.value)
+
+
+def fwd_bwd(ssims_ptr: int, ssims_dtype: int, ssims_len: int, grad_ptr: int, grad_dtype: int,
+            x_ptr: int, x_dtype: int, y_ptr: int, y_dtype: int, qmp_ptr: int,
+            c: int, h: int, w: int, n: int, flags: int, ws_ptr: int, ws_bytes: int, stream: int) -> None:
+    check(load().fssim_fwd_bwd(ssims_ptr or None, ssims_dtype, ssims_len, grad_ptr or None, grad_dtype,
+                               x_ptr or None, x_dtype, y_ptr or None, y_dtype, qmp_ptr or None,
+                               c, h, w, n, flags, ws_ptr or None, ws_bytes, stream or None))

@@ -1,0 +1,46 @@
+"""Builds libfastssim.so in-tree with nvcc for sm_100a (no JIT, no torch extension).
+
+``python build.py`` from any directory, or ``build()`` from Python.  The result
+is ``lib/libfastssim.so`` next to this file; the CUDA runtime is linked
+statically, so the library only needs the NVIDIA driver at run time.
+"""
+from __future__ import annotations
+
+import os
+import subprocess
+import sys
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+ROOT = os.path.dirname(HERE)
+SRC = [os.path.join(HERE, "csrc", "fssim.cu")]
+DEPS = SRC + [os.path.join(HERE, "csrc", "fssim_kernels.cuh"), os.path.join(ROOT, "include", "fastssim.h")]
+OUT = os.path.join(HERE, "lib", "libfastssim.so")
+
+NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
+              "-Xcompiler", "-fPIC", "-shared", "-cudart", "static"]
+
+
+def nvcc() -> str:
+    for cand in (os.environ.get("NVCC"), "/usr/local/cuda/bin/nvcc", "nvcc"):
+        if cand and (os.path.sep not in cand or os.path.exists(cand)):
+            return cand
+    return "nvcc"
+
+
+def build(force: bool = False, verbose: bool = False) -> str:
+    os.makedirs(os.path.dirname(OUT), exist_ok=True)
+    if not force and os.path.exists(OUT):
+        newest = max(os.path.getmtime(p) for p in DEPS)
+        if os.path.getmtime(OUT) >= newest:
+            return OUT
+    cmd = [nvcc(), *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-I", os.path.join(HERE, "csrc"),
+           "-o", OUT, *SRC]
+    if verbose:
+        cmd.insert(1, "-Xptxas=-v")
+        print(" ".join(cmd), flush=True)
+    subprocess.run(cmd, check=True)
+    return OUT
+
+
+if __name__ == "__main__":
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))

@@ -1,0 +1,146 @@
+"""Host driver: the Python mirror of ``_ssim_fwd_bwd!`` (FastCUDASSIM.jl src/core.jl:933-1107).
+
+Canonicalisation, shape checks (``DimensionMismatch``), allocation of missing
+outputs and the scalar unpack stay on the host, as in the reference.  The device
+work - which the reference split over a memset, two kernels and a broadcast - is
+one call into ``libfastssim.so`` (``fssim_fwd_bwd``), which launches one kernel.
+"""
+from __future__ import annotations
+
+import threading
+
+import torch
+
+from . import _native as nat
+from .conversions import (canonicalize_gradient_buffer, canonicalize_image,
+                          decanonicalize_gradient_image, is_column_major, jl_empty, should_unpack)
+
+_DTYPE_CODE = {torch.float32: nat.FLOAT32, torch.float16: nat.FLOAT16, torch.uint8: nat.N0F8,
+               torch.float64: nat.FLOAT64}
+_CODE_DTYPE = {v: k for k, v in _DTYPE_CODE.items()}
+
+# Zero-filled scratch for the per-image reductions, one per (device, stream).
+# Every call leaves its workspace zero-filled again, so it is reused as is.
+_ws_lock = threading.Lock()
+_workspaces: dict[tuple[int, int], torch.Tensor] = {}
+
+
+def _workspace(device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> torch.Tensor | None:
+    if nbytes == 0:
+        return None
+    key = (device.index, stream.cuda_stream)
+    with _ws_lock:
+        ws = _workspaces.get(key)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(max(nbytes, 1 << 16), dtype=torch.uint8, device=device)
+            _workspaces[key] = ws
+        return ws
+
+
+def dtype_code(t: torch.Tensor) -> int:
+    try:
+        return _DTYPE_CODE[t.dtype]
+    except KeyError:
+        raise nat.FastSSIMError(nat.ERR_UNSUPPORTED_DTYPE, f"unsupported element type {t.dtype}") from None
+
+
+def promote_dtype(t1: torch.dtype, t2: torch.dtype) -> torch.dtype:
+    """``promote_type(T1, T2, Float32)`` for the element types this engine accepts
+    (src/core.jl:953-954): Float64 if either is Float64, else Float32 (N0f8 and
+    Float16 promote to Float32)."""
+    return torch.float64 if torch.float64 in (t1, t2) else torch.float32
+
+
+def _require_device_array(name: str, t: torch.Tensor) -> None:
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor in Julia (column-major) layout")
+    if not t.is_cuda:
+        raise ValueError(f"{name} must live on a CUDA device (got {t.device}); CPU arrays are not uploaded")
+    if not is_column_major(t):
+        raise ValueError(f"{name} must be column-major (Julia layout); use conversions.jl_empty/jl_reshape")
+
+
+def ssim_fwd_bwd(ssims, dL_dimgs1, imgs1, imgs2, N_dssims_dQMP, should_zero: bool,
+                 skip_ssim: bool, skip_backward: bool, use_dssim: bool, divide_by_two_in_dssim: bool):
+    """``_ssim_fwd_bwd!`` (src/core.jl:933-1107).  Returns ``(ssims, dL_dimgs1)``.
+
+    Arguments that are ``None`` are allocated (outputs) or not needed (the
+    intermediate buffer: the fused kernel keeps the partial gradients on chip).
+    An allocated ``ssims`` for an input without a batch axis comes back as a
+    Python float (src/conversions.jl:98-106)."""
+    # Shape rules first, as in the reference (src/core.jl:942-984); the device
+    # check comes after them, where the reference would fail on a CPU array.
+    cimgs1 = canonicalize_image(imgs1)
+    cimgs2 = canonicalize_image(imgs2)
+    if tuple(cimgs1.shape) != tuple(cimgs2.shape):
+        raise nat.DimensionMismatch(
+            "The two image batches should have the same dimensions! "
+            f"Received (canonical) sizes {tuple(cimgs1.shape)} and {tuple(cimgs2.shape)}.")
+    c, h, w, b = (int(s) for s in cimgs1.shape)
+    T = promote_dtype(cimgs1.dtype, cimgs2.dtype)
+    device = cimgs1.device
+    flags = 0
+    allocated_ssims = False
+    if not skip_ssim:
+        if ssims is None:
+            ssims = torch.empty(b, dtype=T, device=device)
+            allocated_ssims = True
+            flags |= nat.SHOULD_ZERO
+        else:
+            if tuple(ssims.shape) != (b,):
+                raise nat.DimensionMismatch(
+                    f"Expected the (d)ssims to be a CuVector of length the batch size {b}! "
+                    f"Received size {tuple(ssims.shape)}.")
+            if should_zero:
+                flags |= nat.SHOULD_ZERO
+    else:
+        flags |= nat.SKIP_SSIM
+    if not skip_backward and N_dssims_dQMP is not None:
+        gb = canonicalize_gradient_buffer(N_dssims_dQMP)
+        if tuple(gb.shape) != (h, 3, c, w, b):
+            raise nat.DimensionMismatch(
+                f"Given images in canonical size {(c, h, w, b)}, expected the intermediate gradients buffer "
+                f"N_dssims_dQMP to have size {(h, 3, c, w, b)}, but received {tuple(gb.shape)}!")
+    allocated_grad = False
+    if skip_backward:
+        flags |= nat.SKIP_BACKWARD
+        dl_c = None
+    else:
+        if dL_dimgs1 is None:
+            dl_c = jl_empty((c, h, w, b), T, device)
+            allocated_grad = True
+        else:
+            dl_c = canonicalize_image(dL_dimgs1)
+            if tuple(dl_c.shape) != tuple(cimgs1.shape):
+                raise nat.DimensionMismatch(
+                    "Expected the output gradient dL_dimgs1 to have the same canonical size "
+                    f"{tuple(cimgs1.shape)} as the first input image batch! Instead received (canonical) "
+                    f"size {tuple(dl_c.shape)}.")
+    if use_dssim:
+        flags |= nat.USE_DSSIM
+        if divide_by_two_in_dssim:
+            flags |= nat.DIVIDE_BY_TWO
+    for name, t in (("imgs1", imgs1), ("imgs2", imgs2), ("ssims", None if skip_ssim else ssims),
+                    ("dL_dimgs1", dl_c)):
+        if t is not None:
+            _require_device_array(name, t)
+            if t.device != device:
+                raise ValueError(f"{name} is on {t.device}, expected {device}")
+
+    with torch.cuda.device(device):
+        stream = torch.cuda.current_stream(device)
+        nbytes = nat.workspace_size(c, h, w, b, flags)
+        ws = _workspace(device, stream, nbytes)
+        nat.fwd_bwd(
+            ssims.data_ptr() if not skip_ssim else 0, dtype_code(ssims) if not skip_ssim else nat.FLOAT32,
+            b if skip_ssim else int(ssims.shape[0]),
+            dl_c.data_ptr() if dl_c is not None else 0, dtype_code(dl_c) if dl_c is not None else nat.FLOAT32,
+            cimgs1.data_ptr(), dtype_code(cimgs1), cimgs2.data_ptr(), dtype_code(cimgs2), 0,
+            c, h, w, b, flags, ws.data_ptr() if ws is not None else 0,
+            ws.numel() if ws is not None else 0, stream.cuda_stream)
+
+    if not skip_ssim and allocated_ssims and should_unpack(ssims, imgs1):
+        ssims = ssims.item()           # the reference's blocking scalar read
+    if allocated_grad:
+        dL_dimgs1 = decanonicalize_gradient_image(dl_c, imgs1)
+    return (None if skip_ssim else ssims), dL_dimgs1

@@ -1,0 +1,339 @@
+// C ABI of libfastssim.so: argument checks, launch configuration and the single
+// launch that replaces _ssim_fwd_bwd!'s device work (FastCUDASSIM.jl v0.2.1,
+// src/core.jl:933-1107).  Declarations and the contract live in include/fastssim.h.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <algorithm>
+#include <map>
+#include <mutex>
+
+#include "fastssim.h"
+#include "fssim_kernels.cuh"
+
+namespace {
+
+thread_local int g_status = FSSIM_OK;
+thread_local char g_msg[512] = "";
+
+int fail(int status, const char* fmt, ...)
+{
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(g_msg, sizeof g_msg, fmt, ap);
+    va_end(ap);
+    g_status = status;
+    return status;
+}
+
+int ok()
+{
+    g_status = FSSIM_OK;
+    g_msg[0] = '\0';
+    return FSSIM_OK;
+}
+
+// Gaussian weights, sigma = 1.5, radius 5, evaluated like src/core.jl:40-46:
+// Float32 exp(-0.5 (i/1.5)^2), normalised by their Float32 sum (left to right).
+struct Weights {
+    float k[fssim::TAPS];
+    Weights()
+    {
+        const float sd = 1.5f;
+        float raw[fssim::TAPS];
+        float sum = 0.0f;
+        for (int i = -fssim::RAD; i <= fssim::RAD; ++i) {
+            const float r = static_cast<float>(i) / sd;
+            raw[i + fssim::RAD] = static_cast<float>(std::exp(static_cast<double>(-0.5f * (r * r))));
+        }
+        for (int i = 0; i < fssim::TAPS; ++i) sum += raw[i];
+        for (int i = 0; i < fssim::TAPS; ++i) k[i] = raw[i] / sum;
+    }
+};
+const Weights& weights()
+{
+    static const Weights w;
+    return w;
+}
+
+struct KInfo {
+    const void* fn;
+    int smem;
+    int nt;
+};
+
+template <int NT, bool F, bool WS, bool IO>
+KInfo kinfo()
+{
+    return KInfo{reinterpret_cast<const void*>(&fssim::band_kernel<NT, F, WS, IO>),
+                 fssim::Smem<NT, F, IO>::total, NT};
+}
+
+template <bool IO>
+KInfo kernel_info_io(int nt, bool fused, bool want_ssim)
+{
+    if (fused) {
+        if (want_ssim) {
+            if (nt == 64) return kinfo<64, true, true, IO>();
+            if (nt == 96) return kinfo<96, true, true, IO>();
+            return kinfo<128, true, true, IO>();
+        }
+        if (nt == 64) return kinfo<64, true, false, IO>();
+        if (nt == 96) return kinfo<96, true, false, IO>();
+        return kinfo<128, true, false, IO>();
+    }
+    if (nt == 64) return kinfo<64, false, true, IO>();
+    if (nt == 96) return kinfo<96, false, true, IO>();
+    return kinfo<128, false, true, IO>();
+}
+
+KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io)
+{
+    return f32io ? kernel_info_io<true>(nt, fused, want_ssim) : kernel_info_io<false>(nt, fused, want_ssim);
+}
+
+// Per-device facts, computed once per (device, kernel) under a lock.
+struct DevInfo {
+    int sms = 0;
+    std::map<const void*, int> occ;   // resident CTAs per SM
+};
+std::mutex g_mu;
+std::map<int, DevInfo> g_dev;
+
+int device_facts(const KInfo& ki, int* sms, int* occ)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    std::lock_guard<std::mutex> lk(g_mu);
+    DevInfo& d = g_dev[dev];
+    if (d.sms == 0) {
+        e = cudaDeviceGetAttribute(&d.sms, cudaDevAttrMultiProcessorCount, dev);
+        if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "cudaDeviceGetAttribute: %s", cudaGetErrorString(e));
+    }
+    auto it = d.occ.find(ki.fn);
+    if (it == d.occ.end()) {
+        e = cudaFuncSetAttribute(ki.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ki.smem);
+        if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
+        int o = 0;
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, ki.fn, ki.nt, ki.smem);
+        if (e != cudaSuccess)
+            return fail(FSSIM_ERR_CUDA, "cudaOccupancyMaxActiveBlocksPerMultiprocessor: %s", cudaGetErrorString(e));
+        if (o < 1) o = 1;
+        it = d.occ.emplace(ki.fn, o).first;
+    }
+    *sms = d.sms;
+    *occ = it->second;
+    return FSSIM_OK;
+}
+
+struct Cfg {
+    bool fused = false, want_ssim = false;
+    int nt = 0, T = 0, nb = 0, nseg = 0, L = 0;
+    int64_t cpi = 0, grid = 0;
+    KInfo ki{};
+    size_t ws_counters = 0, ws_bytes = 0;
+};
+
+int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Launch geometry: band height from {54, 86, 118} rows (gradient kernels) or
+// {64, 96, 128} (forward only) to minimise padded rows, then the number of
+// width segments that best fills the GPU (whole waves of resident CTAs
+// versus the 10-20 warm-up columns each extra segment costs).
+int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f32io, Cfg* cfg)
+{
+    Cfg g;
+    g.fused = !(flags & FSSIM_SKIP_BACKWARD);
+    g.want_ssim = !(flags & FSSIM_SKIP_SSIM);
+    if (!g.fused && !g.want_ssim) {
+        *cfg = g;
+        return FSSIM_OK;
+    }
+    const int cands[3] = {64, 96, 128};
+    int64_t best = -1;
+    for (int nt : cands) {
+        const int T = g.fused ? nt - 2 * fssim::RAD : nt;
+        const int64_t nb = cdiv(h, T);
+        const int64_t cost = g.fused ? nb * (4 * nt - 20) : nb * (2 * nt + 3);
+        if (best < 0 || cost <= best) {
+            best = cost;
+            g.nt = nt;
+            g.T = T;
+            g.nb = static_cast<int>(nb);
+        }
+    }
+    g.ki = kernel_info(g.nt, g.fused, g.want_ssim, f32io);
+    int sms = 0, occ = 0;
+    int st = device_facts(g.ki, &sms, &occ);
+    if (st != FSSIM_OK) return st;
+    const int64_t slots = static_cast<int64_t>(sms) * occ;
+    const int64_t base = n * c * g.nb;
+    int64_t best_cost = -1;
+    const int64_t max_seg = std::max<int64_t>(1, cdiv(w, fssim::S));
+    for (int64_t ns = 1; ns <= max_seg; ++ns) {
+        const int64_t L = cdiv(cdiv(w, ns), fssim::S) * fssim::S;
+        if (cdiv(w, L) != ns) continue;
+        const int64_t steps = g.fused ? cdiv(L + 12, fssim::S) + 1 : cdiv(L + 2, fssim::S) + 1;
+        const int64_t waves = cdiv(base * ns, slots);
+        const int64_t cost = waves * steps;
+        if (best_cost < 0 || cost < best_cost) {
+            best_cost = cost;
+            g.nseg = static_cast<int>(ns);
+            g.L = static_cast<int>(L);
+        }
+        if (base * ns > 8 * slots) break;   // further splits only add warm-up work
+    }
+    g.cpi = c * g.nb * g.nseg;
+    g.grid = n * g.cpi;
+    g.ws_counters = ((static_cast<size_t>(n) * sizeof(unsigned) + 255) / 256) * 256;
+    g.ws_bytes = g.want_ssim ? g.ws_counters + static_cast<size_t>(n) * g.cpi * sizeof(double) : 0;
+    *cfg = g;
+    return FSSIM_OK;
+}
+
+bool is_input_dtype(int d) { return d == FSSIM_FLOAT32 || d == FSSIM_FLOAT16 || d == FSSIM_N0F8; }
+bool is_float_dtype(int d) { return d == FSSIM_FLOAT32 || d == FSSIM_FLOAT16 || d == FSSIM_FLOAT64; }
+size_t dsize(int d) { return d == FSSIM_FLOAT32 ? 4 : d == FSSIM_FLOAT16 ? 2 : d == FSSIM_N0F8 ? 1 : 8; }
+bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int check_sizes(int64_t c, int64_t h, int64_t w, int64_t n)
+{
+    if (c < 1 || h < 1 || w < 1 || n < 1)
+        return fail(FSSIM_ERR_INVALID_ARGUMENT, "sizes must be positive, got (c,h,w,n) = (%lld,%lld,%lld,%lld)",
+                    (long long)c, (long long)h, (long long)w, (long long)n);
+    const int64_t lim = (int64_t(1) << 31) - 1;
+    if (c > lim || h > lim || w > lim || n > lim || c * h > lim || c * h * w > (int64_t(1) << 40))
+        return fail(FSSIM_ERR_INVALID_ARGUMENT, "sizes out of range (c,h,w,n) = (%lld,%lld,%lld,%lld)",
+                    (long long)c, (long long)h, (long long)w, (long long)n);
+    return FSSIM_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* fssim_version(void) { return "fastssim 0.1.0 (abi 1, sm_100a)"; }
+
+int fssim_last_error(char* buf, size_t len)
+{
+    if (buf && len) {
+        std::strncpy(buf, g_msg, len - 1);
+        buf[len - 1] = '\0';
+    }
+    return g_status;
+}
+
+int fssim_workspace_size(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, size_t* bytes)
+{
+    if (!bytes) return fail(FSSIM_ERR_INVALID_ARGUMENT, "bytes is NULL");
+    int st = check_sizes(c, h, w, n);
+    if (st != FSSIM_OK) return st;
+    // The launch geometry (and so the workspace) can differ between the
+    // Float32 specialisation and the generic kernels: report the larger need.
+    Cfg g1, g2;
+    st = configure(c, h, w, n, flags, true, &g1);
+    if (st != FSSIM_OK) return st;
+    st = configure(c, h, w, n, flags, false, &g2);
+    if (st != FSSIM_OK) return st;
+    *bytes = std::max(g1.ws_bytes, g2.ws_bytes);
+    return ok();
+}
+
+int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs1, int grad_dtype,
+                  const void* imgs1, int imgs1_dtype, const void* imgs2, int imgs2_dtype, void* qmp,
+                  int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, void* workspace,
+                  size_t workspace_bytes, void* stream)
+{
+    (void)qmp;   // the partial gradients never leave the chip (see fastssim.h)
+    const uint32_t known = FSSIM_SKIP_SSIM | FSSIM_SKIP_BACKWARD | FSSIM_USE_DSSIM | FSSIM_DIVIDE_BY_TWO |
+                           FSSIM_SHOULD_ZERO;
+    if (flags & ~known) return fail(FSSIM_ERR_INVALID_ARGUMENT, "unknown flag bits 0x%x", flags & ~known);
+    int st = check_sizes(c, h, w, n);
+    if (st != FSSIM_OK) return st;
+    if (!imgs1 || !imgs2) return fail(FSSIM_ERR_INVALID_ARGUMENT, "imgs1 and imgs2 must not be NULL");
+    if (!is_input_dtype(imgs1_dtype) || !is_input_dtype(imgs2_dtype))
+        return fail(FSSIM_ERR_UNSUPPORTED_DTYPE, "image dtypes must be FLOAT32, FLOAT16 or N0F8 (got %d, %d)",
+                    imgs1_dtype, imgs2_dtype);
+    if (!aligned(imgs1, dsize(imgs1_dtype)) || !aligned(imgs2, dsize(imgs2_dtype)))
+        return fail(FSSIM_ERR_MISALIGNED, "image pointers must be aligned to their element size");
+    const bool want_ssim = !(flags & FSSIM_SKIP_SSIM);
+    const bool fused = !(flags & FSSIM_SKIP_BACKWARD);
+    if (want_ssim) {
+        if (!ssims) return fail(FSSIM_ERR_INVALID_ARGUMENT, "ssims must not be NULL unless FSSIM_SKIP_SSIM");
+        if (!is_float_dtype(ssims_dtype))
+            return fail(FSSIM_ERR_UNSUPPORTED_DTYPE, "ssims dtype must be FLOAT32, FLOAT64 or FLOAT16 (got %d)",
+                        ssims_dtype);
+        if (ssims_len != n)
+            return fail(FSSIM_ERR_DIMENSION_MISMATCH,
+                        "Expected the (d)ssims to be a vector of length the batch size %lld! Received length %lld.",
+                        (long long)n, (long long)ssims_len);
+        if (!aligned(ssims, dsize(ssims_dtype)))
+            return fail(FSSIM_ERR_MISALIGNED, "ssims must be aligned to its element size");
+    }
+    if (fused) {
+        if (!dL_dimgs1)
+            return fail(FSSIM_ERR_INVALID_ARGUMENT, "dL_dimgs1 must not be NULL unless FSSIM_SKIP_BACKWARD");
+        if (!is_float_dtype(grad_dtype))
+            return fail(FSSIM_ERR_UNSUPPORTED_DTYPE, "gradient dtype must be FLOAT32, FLOAT16 or FLOAT64 (got %d)",
+                        grad_dtype);
+        if (!aligned(dL_dimgs1, dsize(grad_dtype)))
+            return fail(FSSIM_ERR_MISALIGNED, "dL_dimgs1 must be aligned to its element size");
+    }
+    if (!want_ssim && !fused) return ok();   // nothing requested
+
+    const bool f32io = imgs1_dtype == FSSIM_FLOAT32 && imgs2_dtype == FSSIM_FLOAT32 &&
+                       (!fused || grad_dtype == FSSIM_FLOAT32);
+    Cfg g;
+    st = configure(c, h, w, n, flags, f32io, &g);
+    if (st != FSSIM_OK) return st;
+    if (want_ssim) {
+        if (!workspace || workspace_bytes < g.ws_bytes)
+            return fail(FSSIM_ERR_WORKSPACE, "workspace of %zu bytes required, got %zu", g.ws_bytes,
+                        workspace ? workspace_bytes : (size_t)0);
+        if (!aligned(workspace, 256)) return fail(FSSIM_ERR_MISALIGNED, "workspace must be 256-byte aligned");
+    }
+
+    fssim::Params p{};
+    p.x = imgs1;
+    p.y = imgs2;
+    p.grad = fused ? dL_dimgs1 : nullptr;
+    p.ssims = want_ssim ? ssims : nullptr;
+    p.counters = want_ssim ? static_cast<unsigned*>(workspace) : nullptr;
+    p.partials = want_ssim ? reinterpret_cast<double*>(static_cast<char*>(workspace) + g.ws_counters) : nullptr;
+    p.img_elems = c * h * w;
+    p.C = static_cast<int>(c);
+    p.H = static_cast<int>(h);
+    p.W = static_cast<int>(w);
+    p.N = static_cast<int>(n);
+    p.nb = g.nb;
+    p.nseg = g.nseg;
+    p.L = g.L;
+    p.cpi = static_cast<int>(g.cpi);
+    p.xdt = imgs1_dtype;
+    p.ydt = imgs2_dtype;
+    p.gdt = grad_dtype;
+    p.sdt = ssims_dtype;
+    p.should_zero = (flags & FSSIM_SHOULD_ZERO) ? 1 : 0;
+    p.use_dssim = (flags & FSSIM_USE_DSSIM) ? 1 : 0;
+    p.div2 = (flags & FSSIM_DIVIDE_BY_TWO) ? 1 : 0;
+    for (int i = 0; i <= fssim::RAD; ++i) p.kh[i] = weights().k[i];
+    p.C1 = 0.01f * 0.01f;
+    p.C2 = 0.03f * 0.03f;
+    p.npx = static_cast<double>(c * h * w);
+    // src/core.jl:584-589: N_inv = 1/N, or 0.5/N for DSSIM with divide_by_two; the
+    // DSSIM sign (src/core.jl:648) is folded in here.
+    const double scale = ((p.use_dssim && p.div2) ? 0.5 : 1.0) / p.npx;
+    p.gscale = static_cast<float>(p.use_dssim ? -scale : scale);
+
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    void* args[] = {&p};
+    cudaError_t e = cudaLaunchKernel(g.ki.fn, dim3(static_cast<unsigned>(g.grid)), dim3(g.nt), args, g.ki.smem, s);
+    if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
+    return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,506 @@
+// Fused SSIM / DSSIM kernels for sm_100a.
+//
+// Replaces FastCUDASSIM.jl's two CUDA.jl kernels (src/core.jl:147-447 forward,
+// src/core.jl:567-800 backward) and the divide-by-N broadcast
+// (src/core.jl:1123-1157) with ONE launch per call.
+//
+// Decomposition.  A CTA owns one channel c of one image n, a band of T output
+// rows [h0, h0+T) along the contiguous height axis, and a segment of output
+// columns [w0, w0+L) along the width axis.  It streams along the width axis in
+// steps of S = 8 columns:
+//
+//   loader  global (C,H,W,N) -> smem staging, one step ahead through registers
+//           (the element type is converted here: Float32, Float16, N0f8)
+//   F1      h-direction 11-tap Gaussian of the 4 moment images x, y, x^2+y^2, xy
+//           (each thread: 8 consecutive rows of one column; taps from smem)
+//   F2      w-direction 11-tap Gaussian (each thread: one row; the 10 previous
+//           columns stay in registers, so no column is ever recomputed inside a
+//           segment), then the SSIM map and, for gradients, the three partial
+//           derivatives dS/dM, dS/dQ, dS/dP at that pixel (zero outside the image)
+//   B1, B2  the same two passes over the partial-derivative images, then the
+//           combine 2x*K(dQ) + K(dM) + y*K(dP), scaled by +-1/N (or +-0.5/N)
+//
+// With gradients the forward stages run on the band plus a 5-row halo (the
+// backward correlation needs partials there); the width halo costs nothing but
+// the 10+10 warm-up columns of each segment.  Nothing but the inputs, the
+// gradient and one double per CTA ever touches global memory.
+//
+// Only four moment images are convolved, not the reference's five: the SSIM map
+// needs the two variances only through their sum, so E[x^2] and E[y^2] are
+// convolved together as E[x^2 + y^2] (t = E[x^2+y^2] - mx^2 - my^2 + C2).
+//
+// Per-image sums: each CTA writes one double to the workspace; the last CTA of
+// an image (atomic counter) adds them in a fixed order, divides by N and applies
+// the DSSIM transform, so results are bitwise reproducible.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fssim {
+
+constexpr int RAD = 5;              // Gaussian radius (src/core.jl:41)
+constexpr int TAPS = 2 * RAD + 1;   // 11
+constexpr int S = 8;                // columns per streaming step
+constexpr int V = 8;                // rows per thread in the h-direction passes
+constexpr int HIST = 2 * RAD;       // columns of history kept in registers
+constexpr int SP = S + 1;           // staging row stride, in float2 (odd: conflict-free)
+constexpr int FC = S + 1;           // float4 buffer row stride, in float4 (odd: conflict-free)
+
+enum DType { DT_F32 = 0, DT_F16 = 1, DT_U8 = 2, DT_F64 = 3 };
+
+struct Params {
+    const void* x;            // imgs1, canonical (C,H,W,N)
+    const void* y;            // imgs2
+    void* grad;               // dL/dimgs1 (fused kernels with a gradient)
+    void* ssims;              // length-N output (kernels with WANT_SSIM)
+    double* partials;         // workspace: N * cpi doubles
+    unsigned int* counters;   // workspace: N counters, zero between calls
+    int64_t img_elems;        // C*H*W
+    int C, H, W, N;
+    int nb, nseg, L;          // bands, segments, segment length (columns)
+    int cpi;                  // CTAs per image = C * nb * nseg
+    int xdt, ydt, gdt, sdt;   // dtypes of x, y, grad, ssims
+    int should_zero, use_dssim, div2;
+    float kh[RAD + 1];        // Gaussian weights k[0..5] (k[10-i] == k[i]; src/core.jl:40-46)
+    float C1, C2;             // src/core.jl:49-50
+    float gscale;             // +-1/N or +-0.5/N (src/core.jl:584-589, sign for DSSIM)
+    double npx;               // N = C*H*W as a double
+};
+
+__device__ __forceinline__ float rcp_approx(float v)
+{
+    float r;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
+    return r;
+}
+
+// Raw bits of one input element (zero-extended); converted at staging time so
+// that the load's latency is not exposed at the point of issue.
+__device__ __forceinline__ uint32_t ld_raw(const void* base, int dt, int64_t idx)
+{
+    if (dt == DT_F32) return __ldg(reinterpret_cast<const unsigned int*>(base) + idx);
+    if (dt == DT_F16) return __ldg(reinterpret_cast<const unsigned short*>(base) + idx);
+    return __ldg(reinterpret_cast<const unsigned char*>(base) + idx);
+}
+
+__device__ __forceinline__ float cvt_raw(uint32_t r, int dt, const float* lut)
+{
+    if (dt == DT_F32) return __uint_as_float(r);
+    if (dt == DT_F16) return __half2float(__ushort_as_half(static_cast<unsigned short>(r)));
+    return lut[r & 255u];
+}
+
+__device__ __forceinline__ void st_grad(void* base, int dt, int64_t idx, float v)
+{
+    if (dt == DT_F32) reinterpret_cast<float*>(base)[idx] = v;
+    else if (dt == DT_F16) reinterpret_cast<__half*>(base)[idx] = __float2half_rn(v);
+    else reinterpret_cast<double*>(base)[idx] = static_cast<double>(v);
+}
+
+__device__ __forceinline__ double ld_out(const void* base, int dt, int64_t i)
+{
+    if (dt == DT_F32) return reinterpret_cast<const float*>(base)[i];
+    if (dt == DT_F16) return __half2float(reinterpret_cast<const __half*>(base)[i]);
+    return reinterpret_cast<const double*>(base)[i];
+}
+
+__device__ __forceinline__ void st_out(void* base, int dt, int64_t i, double v)
+{
+    if (dt == DT_F32) reinterpret_cast<float*>(base)[i] = static_cast<float>(v);
+    else if (dt == DT_F16) reinterpret_cast<__half*>(base)[i] = __double2half(v);
+    else reinterpret_cast<double*>(base)[i] = v;
+}
+
+// 4-byte asynchronous global->shared copy; a false `valid` zero-fills the
+// destination without reading global memory (src-size 0).
+__device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc, bool valid)
+{
+    const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
+    const int sz = valid ? 4 : 0;
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gsrc), "r"(sz) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait()
+{
+    asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// Shared-memory footprint of one CTA, in bytes (host and device agree on it).
+template <int NT, bool FUSED, bool F32IO>
+struct Smem {
+    static constexpr int R1 = NT;                          // moment / partial rows
+    static constexpr int T = FUSED ? NT - 2 * RAD : NT;    // output rows of a band
+    static constexpr int R2 = R1 + 2 * RAD;                // input rows
+    static constexpr int NRUNB = (T + V - 1) / V;          // runs of the B1 pass
+    static constexpr int QROWS = NRUNB * V + 2 * RAD;      // partial rows incl. zero padding
+    static constexpr int stage_one = R2 * SP * 8;                // one staging buffer
+    static constexpr int stage_bytes = (F32IO ? 2 : 1) * stage_one;   // cp.async path double-buffers
+    static constexpr int f1_bytes = R1 * FC * 16;
+    static constexpr int qmp_bytes = FUSED ? QROWS * FC * 16 : 0;
+    static constexpr int b1_bytes = FUSED ? NT * FC * 16 : 0;
+    static constexpr int lut_bytes = F32IO ? 0 : 256 * 4;
+    static constexpr int red_bytes = (NT / 32 + 2) * 8;
+    static constexpr int total = stage_bytes + f1_bytes + qmp_bytes + b1_bytes + lut_bytes + red_bytes;
+    static_assert(stage_bytes % 16 == 0, "staging must keep 16-byte alignment");
+};
+
+// Reduce a per-thread double over the CTA in a fixed order; result valid in thread 0.
+template <int NT>
+__device__ __forceinline__ double block_sum(double v, double* red)
+{
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+    __syncthreads();
+    double tot = 0.0;
+    if (threadIdx.x == 0) {
+#pragma unroll
+        for (int w = 0; w < NT / 32; ++w) tot += red[w];
+    }
+    return tot;
+}
+
+// Writes this CTA's map sum, and, in the last CTA of the image, the final value.
+template <int NT>
+__device__ __forceinline__ void finish_image(const Params& p, int n, int local_cta, double tsum,
+                                             double* red)
+{
+    const double tot = block_sum<NT>(tsum, red);
+    if (threadIdx.x == 0) {
+        p.partials[(int64_t)n * p.cpi + local_cta] = tot;
+        __threadfence();
+        const unsigned prev = atomicAdd(&p.counters[n], 1u);
+        red[NT / 32] = (prev == static_cast<unsigned>(p.cpi - 1)) ? 1.0 : 0.0;
+    }
+    __syncthreads();
+    if (red[NT / 32] == 0.0) return;
+    __threadfence();
+    double v = 0.0;
+    for (int i = threadIdx.x; i < p.cpi; i += NT) v += __ldcg(&p.partials[(int64_t)n * p.cpi + i]);
+    __syncthreads();   // red[] is reused below
+    const double sum = block_sum<NT>(v, red);
+    if (threadIdx.x == 0) {
+        double s = sum;
+        if (!p.should_zero) s += ld_out(p.ssims, p.sdt, n);
+        s = s / p.npx;                               // src/core.jl:1125-1157
+        if (p.use_dssim) s = p.div2 ? (1.0 - s) * 0.5 : 1.0 - s;
+        st_out(p.ssims, p.sdt, n, s);
+        p.counters[n] = 0u;                          // leave the workspace zeroed
+    }
+}
+
+// F32IO: both inputs and the gradient are Float32 - loads go straight to shared
+// memory with cp.async (double-buffered, two steps ahead) and no conversion;
+// otherwise elements are loaded by type, converted, and staged through registers.
+template <int NT, bool FUSED, bool WANT_SSIM, bool F32IO>
+__global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
+{
+    using SM = Smem<NT, FUSED, F32IO>;
+    constexpr int R1 = SM::R1;
+    constexpr int T = SM::T;
+    constexpr int R2 = SM::R2;
+    constexpr int NRUNB = SM::NRUNB;
+    constexpr int QROWS = SM::QROWS;
+    constexpr int LAG = FUSED ? 2 * RAD : RAD;      // input column/row offset of the stream
+    constexpr int NLOAD = (R2 * S + NT - 1) / NT;  // staged elements per thread per step
+    static_assert(R1 % V == 0 && NT % 32 == 0, "band geometry");
+    static_assert(R1 / V * S == NT, "F1 runs must cover the CTA exactly");
+
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float2* stage = reinterpret_cast<float2*>(smem_raw);
+    float4* f1buf = reinterpret_cast<float4*>(smem_raw + SM::stage_bytes);
+    float4* qmp = reinterpret_cast<float4*>(smem_raw + SM::stage_bytes + SM::f1_bytes);
+    float4* b1buf = reinterpret_cast<float4*>(smem_raw + SM::stage_bytes + SM::f1_bytes + SM::qmp_bytes);
+    float* lut = reinterpret_cast<float*>(smem_raw + SM::stage_bytes + SM::f1_bytes + SM::qmp_bytes +
+                                          SM::b1_bytes);
+    double* red = reinterpret_cast<double*>(smem_raw + SM::total - SM::red_bytes);
+
+    const int tid = threadIdx.x;
+    int64_t blk = blockIdx.x;
+    const int c = static_cast<int>(blk % p.C);
+    blk /= p.C;
+    const int seg = static_cast<int>(blk % p.nseg);
+    blk /= p.nseg;
+    const int band = static_cast<int>(blk % p.nb);
+    const int n = static_cast<int>(blk / p.nb);
+    const int C = p.C, H = p.H, W = p.W;
+    const int h0 = band * T;
+    const int w0 = seg * p.L;
+    const int wend = min(w0 + p.L, W);
+    const int Lc = wend - w0;
+    const int64_t ibase = static_cast<int64_t>(n) * p.img_elems + c;
+    const int ns = FUSED ? (Lc + 12 + S - 1) / S + 1 : (Lc + 2 + S - 1) / S + 1;
+
+    if (!F32IO)
+        for (int i = tid; i < 256; i += NT) lut[i] = __fdiv_rn(static_cast<float>(i), 255.0f);
+    if (FUSED)
+        for (int e = tid; e < (QROWS - R1) * FC; e += NT) qmp[R1 * FC + e] = make_float4(0.f, 0.f, 0.f, 0.f);
+
+    // ---------------- loader: one step of S columns x R2 rows ----------------
+    auto issue_async = [&](int k, float2* buf) {
+#pragma unroll
+        for (int u = 0; u < NLOAD; ++u) {
+            const int e = tid + NT * u;
+            if (e < R2 * S) {
+                const int i = e % R2, j = e / R2;
+                const int hr = h0 - LAG + i;
+                const int wc = w0 - LAG + k * S + j;
+                const bool ok = k < ns && hr >= 0 && hr < H && wc >= 0 && wc < W;
+                const int64_t g = ok ? ibase + static_cast<int64_t>(C) * (hr + static_cast<int64_t>(H) * wc) : 0;
+                float2* d = buf + i * SP + j;
+                cp_async4(&d->x, reinterpret_cast<const float*>(p.x) + g, ok);
+                cp_async4(&d->y, reinterpret_cast<const float*>(p.y) + g, ok);
+            }
+        }
+        cp_async_commit();
+    };
+    uint32_t rx[F32IO ? 1 : NLOAD], ry[F32IO ? 1 : NLOAD];
+    auto issue_loads = [&](int k) {
+#pragma unroll
+        for (int u = 0; u < (F32IO ? 0 : NLOAD); ++u) {
+            const int e = tid + NT * u;
+            rx[u] = 0u;
+            ry[u] = 0u;
+            if (e < R2 * S) {
+                const int i = e % R2, j = e / R2;
+                const int hr = h0 - LAG + i;
+                const int wc = w0 - LAG + k * S + j;
+                if (k < ns && hr >= 0 && hr < H && wc >= 0 && wc < W) {
+                    const int64_t g = ibase + static_cast<int64_t>(C) * (hr + static_cast<int64_t>(H) * wc);
+                    rx[u] = ld_raw(p.x, p.xdt, g);
+                    ry[u] = ld_raw(p.y, p.ydt, g);
+                }
+            }
+        }
+    };
+    auto store_stage = [&]() {
+#pragma unroll
+        for (int u = 0; u < (F32IO ? 0 : NLOAD); ++u) {
+            const int e = tid + NT * u;
+            if (e < R2 * S) {
+                const int i = e % R2, j = e / R2;
+                stage[i * SP + j] = make_float2(cvt_raw(rx[u], p.xdt, lut), cvt_raw(ry[u], p.ydt, lut));
+            }
+        }
+    };
+
+    if (F32IO) {
+        issue_async(0, stage);
+        issue_async(1, stage + SM::R2 * SP);
+        cp_async_wait<1>();
+    } else {
+        issue_loads(0);
+        __syncthreads();   // lut ready
+        store_stage();
+        issue_loads(1);
+    }
+    __syncthreads();
+
+    // F1 / B1 role: column j1 of the step, run q1 of V consecutive rows.
+    const int j1 = tid & (S - 1);
+    const int q1 = tid >> 3;
+    // F2 role: row `tid` of the R1 rows; B2 role: output row `tid` of the band.
+    const int hr2 = h0 - LAG + RAD + tid;               // image row of the F2 row
+    const bool row_in = hr2 >= 0 && hr2 < H;
+    const bool row_owned = row_in && (FUSED ? (tid >= RAD && tid < RAD + T) : true);
+    const int hg = h0 + tid;                            // image row of the B2 row
+    const bool grow_owned = FUSED && tid < T && hg < H;
+
+    float2 hA[HIST], hB[HIST];          // (mx, my), (E[x^2+y^2], E[xy]) history of F1 columns
+    float2 gQM[HIST];                   // (dQ, dM) history of B1 columns
+    float gP[HIST];                     // dP history of B1 columns
+#pragma unroll
+    for (int m = 0; m < HIST; ++m) {
+        hA[m] = make_float2(0.f, 0.f);
+        hB[m] = make_float2(0.f, 0.f);
+        gQM[m] = make_float2(0.f, 0.f);
+        gP[m] = 0.f;
+    }
+    double tsum = 0.0;
+
+    for (int k = 0; k < ns; ++k) {
+        // ---------------- F1: h-direction pass of the 4 moment images ----------------
+        const float2* st = F32IO ? stage + (k & 1) * (SM::R2 * SP) : stage;
+        {
+            float2 aA[V], aB[V];
+#pragma unroll
+            for (int o = 0; o < V; ++o) {
+                aA[o] = make_float2(0.f, 0.f);
+                aB[o] = make_float2(0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < V + 2 * RAD; ++i) {
+                const float2 xy = st[(V * q1 + i) * SP + j1];
+                const float2 pr = __fmul2_rn(make_float2(xy.x, xy.x), xy);        // (x^2, xy)
+                const float2 sb = make_float2(fmaf(xy.y, xy.y, pr.x), pr.y);      // (x^2+y^2, xy)
+#pragma unroll
+                for (int o = 0; o < V; ++o) {
+                    const int tap = i - o;
+                    if (tap >= 0 && tap < TAPS) {
+                        const float2 kk = make_float2(p.kh[tap <= RAD ? tap : 2 * RAD - tap], p.kh[tap <= RAD ? tap : 2 * RAD - tap]);
+                        aA[o] = __ffma2_rn(xy, kk, aA[o]);
+                        aB[o] = __ffma2_rn(sb, kk, aB[o]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int o = 0; o < V; ++o)
+                f1buf[(V * q1 + o) * FC + j1] = make_float4(aA[o].x, aA[o].y, aB[o].x, aB[o].y);
+        }
+        __syncthreads();
+
+        // ---------------- F2: w-direction pass, SSIM map, partials ----------------
+        {
+            // the staging buffer F1 just read is free: refill it two steps ahead
+            if (F32IO) {
+                issue_async(k + 2, stage + (k & 1) * (SM::R2 * SP));
+            } else {
+                store_stage();       // step k+1, held in registers since the last step
+                issue_loads(k + 2);
+            }
+
+            float2 nA[S], nB[S];
+            float ssum = 0.f;
+#pragma unroll
+            for (int o = 0; o < S; ++o) {
+                {   // column o of this step enters the window just before its first use
+                    const float4 v = f1buf[tid * FC + o];
+                    nA[o] = make_float2(v.x, v.y);
+                    nB[o] = make_float2(v.z, v.w);
+                }
+                float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+#pragma unroll
+                for (int tap = 0; tap < TAPS; ++tap) {
+                    const int m = o + tap;
+                    const float2 wa = (m < HIST) ? hA[m] : nA[m - HIST];
+                    const float2 wb = (m < HIST) ? hB[m] : nB[m - HIST];
+                    const float2 kk = make_float2(p.kh[tap <= RAD ? tap : 2 * RAD - tap], p.kh[tap <= RAD ? tap : 2 * RAD - tap]);
+                    a = __ffma2_rn(wa, kk, a);
+                    b = __ffma2_rn(wb, kk, b);
+                }
+                const float mx = a.x, my = a.y, qs = b.x, pxy = b.y;
+                const float2 sq = __fmul2_rn(a, a);                  // (mx^2, my^2)
+                const float mxy = mx * my;
+                const float sumsq = sq.x + sq.y;
+                const float z = sumsq + p.C1;                        // mx^2 + my^2 + C1
+                const float t = (qs - sumsq) + p.C2;                 // vx + vy + C2
+                const float ax = fmaf(2.f, mxy, p.C1);               // 2 mx my + C1
+                const float by = fmaf(2.f, pxy - mxy, p.C2);         // 2 cov + C2
+                const float inv = rcp_approx(z * t);
+                const float s = (ax * by) * inv;
+                const int wc = w0 - LAG + k * S - RAD + o;           // image column of this pixel
+                if (WANT_SSIM) {
+                    if (row_owned && wc >= w0 && wc < wend) ssum += s;
+                }
+                if (FUSED) {
+                    // dS/dQ = -s/t, dS/dM = 2/(zt) ((by-ax) my + s (z-t) mx), dS/dP = 2 ax/(zt)
+                    // (src/core.jl:384-388; docs/src/math.md, "Gradients")
+                    const float inv2 = 2.f * inv;
+                    const float dq = -(s * z) * inv;
+                    const float dm = inv2 * fmaf(by - ax, my, (s * (z - t)) * mx);
+                    const float dp = ax * inv2;
+                    const bool in_img = row_in && wc >= 0 && wc < W;
+                    qmp[tid * FC + o] = in_img ? make_float4(dq, dm, dp, 0.f) : make_float4(0.f, 0.f, 0.f, 0.f);
+                }
+            }
+            if (WANT_SSIM) tsum += static_cast<double>(ssum);
+#pragma unroll
+            for (int m = 0; m < HIST; ++m) {
+                const int src = m + S;
+                hA[m] = (src < HIST) ? hA[src] : nA[src - HIST];
+                hB[m] = (src < HIST) ? hB[src] : nB[src - HIST];
+            }
+            if (F32IO) cp_async_wait<1>();   // step k+1 has landed (k+2 may still fly)
+        }
+        __syncthreads();
+
+        if (FUSED) {
+            // ---------------- B1: h-direction pass of the partials ----------------
+            if (q1 < NRUNB) {
+                float2 aQM[V];
+                float aP[V];
+#pragma unroll
+                for (int o = 0; o < V; ++o) {
+                    aQM[o] = make_float2(0.f, 0.f);
+                    aP[o] = 0.f;
+                }
+#pragma unroll
+                for (int i = 0; i < V + 2 * RAD; ++i) {
+                    const float4 v = qmp[(V * q1 + i) * FC + j1];
+                    const float2 qm = make_float2(v.x, v.y);
+#pragma unroll
+                    for (int o = 0; o < V; ++o) {
+                        const int tap = i - o;
+                        if (tap >= 0 && tap < TAPS) {
+                            aQM[o] = __ffma2_rn(qm, make_float2(p.kh[tap <= RAD ? tap : 2 * RAD - tap], p.kh[tap <= RAD ? tap : 2 * RAD - tap]), aQM[o]);
+                            aP[o] = fmaf(v.z, p.kh[tap <= RAD ? tap : 2 * RAD - tap], aP[o]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int o = 0; o < V; ++o)
+                    b1buf[(V * q1 + o) * FC + j1] = make_float4(aQM[o].x, aQM[o].y, aP[o], 0.f);
+            }
+            __syncthreads();
+
+            // ---------------- B2: w-direction pass and the combine ----------------
+            {
+                float2 nQM[S];
+                float nP[S];
+#pragma unroll
+                for (int o = 0; o < S; ++o) {
+                    {
+                        const float4 v = b1buf[tid * FC + o];
+                        nQM[o] = make_float2(v.x, v.y);
+                        nP[o] = v.z;
+                    }
+                    float2 a = make_float2(0.f, 0.f);
+                    float bp = 0.f;
+#pragma unroll
+                    for (int tap = 0; tap < TAPS; ++tap) {
+                        const int m = o + tap;
+                        const float2 wq = (m < HIST) ? gQM[m] : nQM[m - HIST];
+                        const float wp = (m < HIST) ? gP[m] : nP[m - HIST];
+                        a = __ffma2_rn(wq, make_float2(p.kh[tap <= RAD ? tap : 2 * RAD - tap], p.kh[tap <= RAD ? tap : 2 * RAD - tap]), a);
+                        bp = fmaf(wp, p.kh[tap <= RAD ? tap : 2 * RAD - tap], bp);
+                    }
+                    const int wc = w0 - LAG + k * S - 2 * RAD + o;
+                    if (grow_owned && wc >= w0 && wc < wend) {
+                        const int64_t g = ibase + static_cast<int64_t>(C) * (hg + static_cast<int64_t>(H) * wc);
+                        float xv, yv;
+                        if (F32IO) {
+                            xv = __ldg(reinterpret_cast<const float*>(p.x) + g);
+                            yv = __ldg(reinterpret_cast<const float*>(p.y) + g);
+                        } else {
+                            xv = cvt_raw(ld_raw(p.x, p.xdt, g), p.xdt, lut);
+                            yv = cvt_raw(ld_raw(p.y, p.ydt, g), p.ydt, lut);
+                        }
+                        // src/core.jl:773-782: (2 x K(dQ) + K(dM) + y K(dP)) * N_inv
+                        const float gv = fmaf(yv, bp, fmaf(2.f * xv, a.x, a.y)) * p.gscale;
+                        if (F32IO) reinterpret_cast<float*>(p.grad)[g] = gv;
+                        else st_grad(p.grad, p.gdt, g, gv);
+                    }
+                }
+#pragma unroll
+                for (int m = 0; m < HIST; ++m) {
+                    const int src = m + S;
+                    gQM[m] = (src < HIST) ? gQM[src] : nQM[src - HIST];
+                    gP[m] = (src < HIST) ? gP[src] : nP[src - HIST];
+                }
+            }
+            // No barrier here: the next step writes f1buf (last read before the F2
+            // barrier), the staging buffer (read before the F1 barrier), qmp (read
+            // before the B1 barrier) and b1buf only after two more barriers.
+        }
+    }
+
+    if (WANT_SSIM) {
+        const int local_cta = (band * p.nseg + seg) * p.C + c;
+        finish_image<NT>(p, n, local_cta, tsum, red);
+    }
+}
+
+}  // namespace fssim

@@ -1,0 +1,117 @@
+/*
+ * fastssim.h - C ABI of the B200 (sm_100a) SSIM / DSSIM engine.
+ *
+ * One shared library, libfastssim.so, replaces the two CUDA.jl kernels of
+ * FastCUDASSIM.jl v0.2.1 and their launch sites.  Every exported Julia function
+ * of that package (src/interface.jl:31-338) funnels into
+ *
+ *     _ssim_fwd_bwd!(ssims, dL_dimgs1, imgs1, imgs2, N_dssims_dQMP, should_zero,
+ *                    Val(skip_ssim), Val(skip_backward), use_dssim, divide_by_two)
+ *                                                      (src/core.jl:933-1107)
+ *
+ * and fssim_fwd_bwd() below is the device-side half of that function: the Julia
+ * side keeps canonicalisation, DimensionMismatch errors, allocation and the
+ * scalar unpack (src/conversions.jl), and calls this entry point where the
+ * reference issued its @cuda launches (src/core.jl:996, :1059) and its
+ * broadcast divide (src/core.jl:1033).
+ *
+ * Conventions shared by all entry points
+ *  - Image batches are canonical (C, H, W, N) column-major arrays: element
+ *    (c, h, w, n) lives at c + C*(h + H*(w + W*n))  (src/core.jl:898-908).
+ *  - All pointers are device pointers on the current CUDA device.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream).  The library
+ *    launches only on that stream and never synchronises it.
+ *  - The library allocates no device memory.  Scratch space for the per-image
+ *    reductions is the caller's `workspace` (size from fssim_workspace_size);
+ *    it must be zero-filled once before its first use, and every call leaves
+ *    it zero-filled again.
+ *  - Return value: FSSIM_OK (0) or a nonzero fssim_status; the message of the
+ *    last error on the calling thread is available from fssim_last_error().
+ */
+#ifndef FASTSSIM_H
+#define FASTSSIM_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define FSSIM_ABI_VERSION 1
+
+/* Element types.  FSSIM_N0F8 is FixedPointNumbers' N0f8: a raw byte b read as
+ * the Float32 value b/255 (correctly rounded). */
+typedef enum fssim_dtype {
+    FSSIM_FLOAT32 = 0,
+    FSSIM_FLOAT16 = 1,
+    FSSIM_N0F8 = 2,
+    FSSIM_FLOAT64 = 3
+} fssim_dtype;
+
+/* Flags of fssim_fwd_bwd, one per argument of _ssim_fwd_bwd! (src/core.jl:933-940). */
+enum fssim_flags {
+    FSSIM_SKIP_SSIM = 1u << 0,      /* Val(skip_ssim): do not produce the (D)SSIM values      */
+    FSSIM_SKIP_BACKWARD = 1u << 1,  /* Val(skip_backward): do not produce dL/dimgs1           */
+    FSSIM_USE_DSSIM = 1u << 2,      /* use_dssim: L = 1 - SSIM (or (1 - SSIM)/2)               */
+    FSSIM_DIVIDE_BY_TWO = 1u << 3,  /* divide_by_two_in_dssim                                  */
+    FSSIM_SHOULD_ZERO = 1u << 4     /* should_zero: ignore the previous contents of `ssims`    */
+};
+
+typedef enum fssim_status {
+    FSSIM_OK = 0,
+    FSSIM_ERR_INVALID_ARGUMENT = 1,   /* null pointer, nonpositive size, unknown flag          */
+    FSSIM_ERR_DIMENSION_MISMATCH = 2, /* e.g. ssims_len != N (the reference's DimensionMismatch) */
+    FSSIM_ERR_UNSUPPORTED_DTYPE = 3,  /* dtype code not accepted for that argument             */
+    FSSIM_ERR_WORKSPACE = 4,          /* workspace missing or smaller than fssim_workspace_size */
+    FSSIM_ERR_MISALIGNED = 5,         /* a pointer not aligned to its element size             */
+    FSSIM_ERR_CUDA = 6                /* a CUDA runtime error (message has the details)        */
+} fssim_status;
+
+/* Library version string, e.g. "fastssim 0.1.0 (abi 1, sm_100a)". */
+const char* fssim_version(void);
+
+/* Copies the last error message of the calling thread into buf (NUL-terminated,
+ * truncated to len).  Returns the status code of that error (FSSIM_OK if none). */
+int fssim_last_error(char* buf, size_t len);
+
+/* Bytes of workspace that fssim_fwd_bwd needs for these sizes and flags on the
+ * current device.  Replaces no reference interface: the reference reduced with
+ * float atomics into `ssims` (src/core.jl:412-440) and divided in a second
+ * launch (src/core.jl:1123-1157); this engine reduces deterministically in one
+ * launch and keeps its per-tile partial sums in the workspace. */
+int fssim_workspace_size(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags,
+                         size_t* bytes);
+
+/*
+ * (D)SSIM of two image batches and/or its gradient with respect to the first.
+ * Device half of _ssim_fwd_bwd! (src/core.jl:933-1107): one fused launch per call.
+ *
+ *  ssims        length-N vector of (D)SSIM values (dtype FLOAT32, FLOAT64 or FLOAT16).
+ *               Required unless FSSIM_SKIP_SSIM.  Without FSSIM_SHOULD_ZERO the
+ *               previous contents are added to the map sums before the division,
+ *               as the reference's accumulation into N_ssims does (src/core.jl:919-922).
+ *  ssims_len    must equal n (src/core.jl:967-969).
+ *  dL_dimgs1    gradient, canonical (C,H,W,N) (dtype FLOAT32 or FLOAT16).  Required
+ *               unless FSSIM_SKIP_BACKWARD.
+ *  imgs1, imgs2 canonical (C,H,W,N) inputs (dtype FLOAT32, FLOAT16 or N0F8 each).
+ *  qmp          the reference's N_dssims_dQMP buffer (h,3,c,w,n).  Accepted for
+ *               interface parity and never read or written: the fused kernel keeps
+ *               the partial gradients on chip.  May be NULL.
+ *  workspace    >= fssim_workspace_size() bytes, zero-filled before first use.
+ */
+int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len,
+                  void* dL_dimgs1, int grad_dtype,
+                  const void* imgs1, int imgs1_dtype,
+                  const void* imgs2, int imgs2_dtype,
+                  void* qmp,
+                  int64_t c, int64_t h, int64_t w, int64_t n,
+                  uint32_t flags,
+                  void* workspace, size_t workspace_bytes,
+                  void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FASTSSIM_H */

@@ -1,0 +1,62 @@
+"""The C ABI library loads without a GPU and exports every symbol include/fastssim.h declares."""
+import ctypes
+import os
+import re
+
+import pytest
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def declared_symbols():
+    with open(os.path.join(ROOT, "include", "fastssim.h")) as f:
+        text = f.read()
+    return sorted(set(re.findall(r"^\s*(?:const\s+)?[a-z_ ]+\*?\s*(fssim_\w+)\s*\(", text, re.M)))
+
+
+def test_header_declares_the_entry_points():
+    syms = declared_symbols()
+    for s in ("fssim_version", "fssim_last_error", "fssim_workspace_size", "fssim_fwd_bwd"):
+        assert s in syms
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    lib = pkg._native.load()
+    for s in declared_symbols():
+        assert hasattr(lib, s), s
+    assert set(pkg._native.EXPORTED_SYMBOLS) <= set(declared_symbols())
+
+
+def test_version_and_error_channel(pkg):
+    assert pkg._native.version().startswith("fastssim")
+    lib = pkg._native.load()
+    # argument errors are reported before any CUDA call
+    st = lib.fssim_fwd_bwd(None, 0, 1, None, 0, None, 0, None, 0, None, 1, 1, 1, 1, 0, None, 0, None)
+    assert st == pkg._native.ERR_INVALID_ARGUMENT
+    code, msg = pkg._native.last_error()
+    assert code == st and "NULL" in msg
+    st = lib.fssim_fwd_bwd(None, 0, 1, None, 0, ctypes.c_void_p(16), 0, ctypes.c_void_p(16), 0, None,
+                           0, 1, 1, 1, 0, None, 0, None)
+    assert st == pkg._native.ERR_INVALID_ARGUMENT
+    st = lib.fssim_fwd_bwd(None, 0, 1, None, 0, ctypes.c_void_p(16), 3, ctypes.c_void_p(16), 0, None,
+                           1, 1, 1, 1, 0, None, 0, None)
+    assert st == pkg._native.ERR_UNSUPPORTED_DTYPE
+    st = lib.fssim_fwd_bwd(ctypes.c_void_p(16), 0, 2, None, 0, ctypes.c_void_p(16), 0, ctypes.c_void_p(16), 0,
+                           None, 1, 1, 1, 1, pkg._native.SKIP_BACKWARD, None, 0, None)
+    assert st == pkg._native.ERR_DIMENSION_MISMATCH
+    with pytest.raises(pkg.DimensionMismatch):
+        pkg._native.check(st)
+    st = lib.fssim_fwd_bwd(None, 0, 1, None, 0, ctypes.c_void_p(16), 0, ctypes.c_void_p(16), 0, None,
+                           1, 1, 1, 1, 1 << 9, None, 0, None)
+    assert st == pkg._native.ERR_INVALID_ARGUMENT
+    st = lib.fssim_fwd_bwd(None, 0, 1, None, 0, ctypes.c_void_p(17), 0, ctypes.c_void_p(16), 0, None,
+                           1, 1, 1, 1, 0, None, 0, None)
+    assert st == pkg._native.ERR_MISALIGNED
+
+
+def test_nothing_requested_is_a_no_op(pkg):
+    lib = pkg._native.load()
+    flags = pkg._native.SKIP_SSIM | pkg._native.SKIP_BACKWARD
+    st = lib.fssim_fwd_bwd(None, 0, 1, None, 0, ctypes.c_void_p(16), 0, ctypes.c_void_p(16), 0, None,
+                           3, 8, 8, 2, flags, None, 0, None)
+    assert st == pkg._native.OK

@@ -1,0 +1,179 @@
+"""Parity of the CUDA path (through the C ABI) with the CPU oracle on seeded inputs.
+
+Tolerances: per-image (D)SSIM within 1e-5 absolute; the
+gradient within 1e-4 relative L2, against the single-precision oracle (the
+reference's operation order) and against the float64 oracle.
+"""
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+SSIM_ATOL = 1e-5
+GRAD_RTOL_L2 = 1e-4
+
+
+def _syn(pkg):
+    return __import__(pkg.__name__ + ".synthetic", fromlist=["x"])
+
+
+def _rel_l2(a, b):
+    a = np.asarray(a, np.float64)
+    b = np.asarray(b, np.float64)
+    return float(np.linalg.norm(a - b) / max(np.linalg.norm(b), 1e-30))
+
+
+def _run(pkg, x, y, *, mode, dssim=False, div2=False, grad_dtype=torch.float32):
+    """mode: 'fwd' (ssim!/dssim!), 'both' (*_with_gradient!), 'grad' (*_gradient!)."""
+    xt, yt = pkg.jl_from_numpy(x), pkg.jl_from_numpy(y)
+    C, H, W, N = x.shape
+    vals = grad = None
+    if mode == "fwd":
+        out = torch.empty(N, dtype=torch.float32, device="cuda")
+        if dssim:
+            pkg.dssim_(out, xt, yt, True, div2)
+        else:
+            pkg.ssim_(out, xt, yt)
+        vals = out
+    else:
+        g = pkg.jl_empty((C, H, W, N), grad_dtype)
+        if mode == "both":
+            out = torch.empty(N, dtype=torch.float32, device="cuda")
+            if dssim:
+                pkg.dssim_with_gradient_(out, g, xt, yt, None, True, div2)
+            else:
+                pkg.ssim_with_gradient_(out, g, xt, yt, None, True)
+            vals = out
+        else:
+            if dssim:
+                pkg.dssim_gradient_(g, xt, yt, None, div2)
+            else:
+                pkg.ssim_gradient_(g, xt, yt, None)
+        grad = g
+    torch.cuda.synchronize()
+    v = None if vals is None else vals.cpu().numpy().astype(np.float64)
+    gr = None if grad is None else pkg.jl_to_numpy(grad).astype(np.float64)
+    return v, gr
+
+
+def _flags(orc, dssim, div2):
+    return (orc.USE_DSSIM if dssim else 0) | (orc.DIVIDE_BY_TWO if (dssim and div2) else 0)
+
+
+SHAPES = [
+    ("fullhd_1ch_crop", (1, 135, 240, 1), 0.1),
+    ("fullhd_3ch_crop", (3, 135, 240, 1), 0.05),
+    ("batch_3x256x256", (3, 256, 256, 3), None),
+    ("odd_3x1023x767", (3, 1023, 767, 1), 0.1),
+    ("odd_1x37x5", (1, 37, 5, 1), None),
+    ("single_px", (1, 1, 1, 2), None),
+    ("c2_odd", (2, 57, 33, 3), 0.1),
+    ("c4_rgba", (4, 40, 129, 2), 0.1),
+    ("c5_general", (5, 31, 20, 1), None),
+    ("tall_narrow", (1, 600, 12, 1), 0.2),
+    ("short_wide", (1, 9, 700, 1), 0.2),
+    ("h512", (3, 512, 200, 1), 0.1),
+]
+
+
+@pytest.mark.parametrize("name,shape,noise", SHAPES, ids=[s[0] for s in SHAPES])
+def test_fused_ssim_and_gradient_vs_oracle(pkg, orc, name, shape, noise):
+    x, y = _syn(pkg).host_pair(17, shape, noise)
+    v, g = _run(pkg, x, y, mode="both")
+    rv, rg = orc.ssim(x, y, precision="f32")
+    dv, dg = orc.ssim(x, y, precision="f64")
+    assert np.max(np.abs(v - rv)) <= SSIM_ATOL, (v, rv)
+    assert np.max(np.abs(v - dv)) <= SSIM_ATOL, (v, dv)
+    assert _rel_l2(g, rg) <= GRAD_RTOL_L2
+    assert _rel_l2(g, dg) <= GRAD_RTOL_L2
+
+
+@pytest.mark.parametrize("name,shape,noise", SHAPES, ids=[s[0] for s in SHAPES])
+def test_forward_only_vs_oracle(pkg, orc, name, shape, noise):
+    x, y = _syn(pkg).host_pair(23, shape, noise)
+    v, _ = _run(pkg, x, y, mode="fwd")
+    rv, _ = orc.ssim(x, y, flags=orc.SKIP_BACKWARD, precision="f64")
+    assert np.max(np.abs(v - rv)) <= SSIM_ATOL, (v, rv)
+
+
+@pytest.mark.parametrize("dssim,div2", [(False, False), (True, False), (True, True)])
+@pytest.mark.parametrize("mode", ["fwd", "both", "grad"])
+def test_flag_combinations(pkg, orc, dssim, div2, mode):
+    x, y = _syn(pkg).host_pair(5, (3, 70, 90, 2), 0.1)
+    v, g = _run(pkg, x, y, mode=mode, dssim=dssim, div2=div2)
+    rv, rg = orc.ssim(x, y, flags=_flags(orc, dssim, div2), precision="f64")
+    if v is not None:
+        assert np.max(np.abs(v - rv)) <= SSIM_ATOL
+    if g is not None:
+        assert _rel_l2(g, rg) <= GRAD_RTOL_L2
+
+
+@pytest.mark.parametrize("xdt,ydt", [(np.uint8, np.uint8), (np.float16, np.float16), (np.uint8, np.float32),
+                                     (np.float32, np.float16), (np.float16, np.uint8)])
+def test_input_dtypes_converted_in_kernel(pkg, orc, xdt, ydt):
+    """Config-4 style inputs: N0f8 and Float16 converted in-kernel, accumulated in Float32."""
+    syn = _syn(pkg)
+    shape = (3, 160, 150, 2)
+    x8, y8 = syn.host_pair(41, shape, 0.1, dtype=np.uint8)
+    xf, yf = syn.host_pair(41, shape, 0.1)
+    x = x8 if xdt == np.uint8 else xf.astype(xdt)
+    y = y8 if ydt == np.uint8 else yf.astype(ydt)
+    x, y = np.asfortranarray(x), np.asfortranarray(y)
+    v, g = _run(pkg, x, y, mode="both")
+    rv, rg = orc.ssim(x, y, precision="f32")
+    assert np.max(np.abs(v - rv)) <= SSIM_ATOL
+    assert _rel_l2(g, rg) <= GRAD_RTOL_L2
+
+
+def test_float16_gradient_output(pkg, orc):
+    """test/eltypes.jl:28-36: a Float16 gradient buffer is within 1e-3 of Float32."""
+    x, y = _syn(pkg).host_pair(9, (3, 128, 96, 1), 0.1)
+    _, g16 = _run(pkg, x, y, mode="grad", dssim=True, grad_dtype=torch.float16)
+    _, g32 = _run(pkg, x, y, mode="grad", dssim=True)
+    assert np.max(np.abs(g16 - g32)) < 1e-3
+    _, rg = orc.ssim(x, y, flags=orc.USE_DSSIM)
+    assert np.max(np.abs(g16 - rg)) < 1e-3
+
+
+@pytest.mark.parametrize("sdt", [torch.float64, torch.float16])
+def test_output_vector_dtypes(pkg, orc, sdt):
+    x, y = _syn(pkg).host_pair(10, (1, 50, 60, 3), 0.1)
+    xt, yt = pkg.jl_from_numpy(x), pkg.jl_from_numpy(y)
+    out = torch.zeros(3, dtype=sdt, device="cuda")
+    pkg.ssim_(out, xt, yt)
+    rv, _ = orc.ssim(x, y, flags=orc.SKIP_BACKWARD, precision="f64")
+    tol = SSIM_ATOL if sdt == torch.float64 else 1e-3
+    assert np.max(np.abs(out.cpu().double().numpy() - rv)) <= tol
+
+
+def test_should_zero_false_accumulates(pkg, orc):
+    """src/core.jl:919-922: without zeroing, the previous contents join the sum."""
+    x, y = _syn(pkg).host_pair(12, (2, 40, 30, 2), 0.1)
+    xt, yt = pkg.jl_from_numpy(x), pkg.jl_from_numpy(y)
+    npx = 2 * 40 * 30
+    pre = torch.tensor([3.0, -5.0], dtype=torch.float64, device="cuda")
+    out = pre.clone()
+    pkg.ssim_(out, xt, yt, False)
+    rv, _ = orc.ssim(x, y, flags=orc.SKIP_BACKWARD, precision="f64")
+    np.testing.assert_allclose(out.cpu().numpy(), pre.cpu().numpy() / npx + rv, atol=SSIM_ATOL)
+
+
+def test_bitwise_deterministic(pkg):
+    x, y = _syn(pkg).host_pair(13, (3, 200, 170, 4), 0.1)
+    a = _run(pkg, x, y, mode="both")
+    b = _run(pkg, x, y, mode="both")
+    np.testing.assert_array_equal(a[0], b[0])
+    np.testing.assert_array_equal(a[1], b[1])
+
+
+def test_golden_scipy_cases(pkg, golden):
+    _, cases = golden
+    for name, c in cases.items():
+        flags = int(c["flags"])
+        dssim, div2 = bool(flags & 4), bool(flags & 8)
+        v, g = _run(pkg, c["x"], c["y"], mode="both", dssim=dssim, div2=div2)
+        assert np.max(np.abs(v - c["vals"])) <= SSIM_ATOL, name
+        # smooth ramps: the Float32 algorithm itself sits ~8e-5 from float64 there
+        tol = 2e-4 if name.startswith("ramps") else GRAD_RTOL_L2
+        assert _rel_l2(g, c["grad"]) <= tol, (name, _rel_l2(g, c["grad"]))
