@@ -380,14 +380,22 @@ def profile_case(args):
     x, y = syn.device_pair(shape, NOISE)
     s = torch.empty(64, dtype=torch.float32, device="cuda")
     g = pkg.jl_empty(shape, torch.float32)
-    for _ in range(args.warmup + args.steps):
+    def launch():
         if args.profile_case == "fused":
             pkg.ssim_with_gradient_(s, g, x, y, None, True)
         else:
             pkg.ssim_(s, x, y)
+    for _ in range(args.warmup):
+        launch()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        launch()
+    b.record()
     torch.cuda.synchronize()
+    ms = a.elapsed_time(b) / max(args.steps, 1)
     print(json.dumps({"profile_case": args.profile_case, "launches": args.warmup + args.steps,
-                      "ssim0": float(s[0])}))
+                      "ms_per_launch": ms, "gelem_per_s": 64 * C * H * W / ms / 1e6, "ssim0": float(s[0])}))
     return 0
 
 

@@ -9,7 +9,8 @@ import ctypes
 import os
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "lib", "libfastssim.so")
+# FASTSSIM_LIB selects another build of the same library (e.g. a tuning variant).
+LIB_PATH = os.environ.get("FASTSSIM_LIB") or os.path.join(_HERE, "lib", "libfastssim.so")
 
 # enum fssim_dtype
 FLOAT32, FLOAT16, N0F8, FLOAT64 = 0, 1, 2, 3

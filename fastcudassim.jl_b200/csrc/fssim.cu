@@ -63,36 +63,43 @@ struct KInfo {
     const void* fn;
     int smem;
     int nt;
+    int s;
 };
 
-template <int NT, bool F, bool WS, bool IO>
+// Kernel variants: band height NT (threads), step width S (columns), with or
+// without the gradient, with or without the SSIM reduction, Float32 I/O or not.
+template <int NT, int S, bool F, bool WS, bool IO>
 KInfo kinfo()
 {
-    return KInfo{reinterpret_cast<const void*>(&fssim::band_kernel<NT, F, WS, IO>),
-                 fssim::Smem<NT, F, IO>::total, NT};
+    return KInfo{reinterpret_cast<const void*>(&fssim::band_kernel<NT, S, F, WS, IO>),
+                 fssim::Geo<NT, S, F, IO>::total, NT, S};
 }
 
-template <bool IO>
-KInfo kernel_info_io(int nt, bool fused, bool want_ssim)
+template <int S, bool IO>
+KInfo kernel_info_s(int nt, bool fused, bool want_ssim)
 {
     if (fused) {
         if (want_ssim) {
-            if (nt == 64) return kinfo<64, true, true, IO>();
-            if (nt == 96) return kinfo<96, true, true, IO>();
-            return kinfo<128, true, true, IO>();
+            if (nt == 64) return kinfo<64, S, true, true, IO>();
+            return kinfo<96, S, true, true, IO>();
         }
-        if (nt == 64) return kinfo<64, true, false, IO>();
-        if (nt == 96) return kinfo<96, true, false, IO>();
-        return kinfo<128, true, false, IO>();
+        if (nt == 64) return kinfo<64, S, true, false, IO>();
+        return kinfo<96, S, true, false, IO>();
     }
-    if (nt == 64) return kinfo<64, false, true, IO>();
-    if (nt == 96) return kinfo<96, false, true, IO>();
-    return kinfo<128, false, true, IO>();
+    if (nt == 64) return kinfo<64, S, false, true, IO>();
+    if (nt == 96) return kinfo<96, S, false, true, IO>();
+    return kinfo<128, S, false, true, IO>();
 }
 
+// Float32 I/O streams 16 columns per step (cp.async staging); the converting
+// kernels stream 8 (their staging goes through registers).
+#ifndef FSSIM_F32_STEP
+#define FSSIM_F32_STEP 16
+#endif
 KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io)
 {
-    return f32io ? kernel_info_io<true>(nt, fused, want_ssim) : kernel_info_io<false>(nt, fused, want_ssim);
+    return f32io ? kernel_info_s<FSSIM_F32_STEP, true>(nt, fused, want_ssim)
+                 : kernel_info_s<8, false>(nt, fused, want_ssim);
 }
 
 // Per-device facts, computed once per (device, kernel) under a lock.
@@ -153,9 +160,14 @@ int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f
         *cfg = g;
         return FSSIM_OK;
     }
-    const int cands[3] = {64, 96, 128};
+    // Gradient kernels: bands of 54 or 86 rows; forward only: 64, 96 or 128 rows.
+    const int cands_fused[2] = {64, 96};
+    const int cands_fwd[3] = {64, 96, 128};
+    const int* cands = g.fused ? cands_fused : cands_fwd;
+    const int ncand = g.fused ? 2 : 3;
     int64_t best = -1;
-    for (int nt : cands) {
+    for (int ci = 0; ci < ncand; ++ci) {
+        const int nt = cands[ci];
         const int T = g.fused ? nt - 2 * fssim::RAD : nt;
         const int64_t nb = cdiv(h, T);
         const int64_t cost = g.fused ? nb * (4 * nt - 20) : nb * (2 * nt + 3);
@@ -173,11 +185,13 @@ int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f
     const int64_t slots = static_cast<int64_t>(sms) * occ;
     const int64_t base = n * c * g.nb;
     int64_t best_cost = -1;
-    const int64_t max_seg = std::max<int64_t>(1, cdiv(w, fssim::S));
+    const int S = g.ki.s;
+    const int lag2 = g.fused ? 4 * fssim::RAD : 2 * fssim::RAD;   // warm-up + drain columns
+    const int64_t max_seg = std::max<int64_t>(1, cdiv(w, S));
     for (int64_t ns = 1; ns <= max_seg; ++ns) {
-        const int64_t L = cdiv(cdiv(w, ns), fssim::S) * fssim::S;
+        const int64_t L = cdiv(cdiv(w, ns), S) * S;
         if (cdiv(w, L) != ns) continue;
-        const int64_t steps = g.fused ? cdiv(L + 12, fssim::S) + 1 : cdiv(L + 2, fssim::S) + 1;
+        const int64_t steps = (L + lag2 - 1) / S + 1;
         const int64_t waves = cdiv(base * ns, slots);
         const int64_t cost = waves * steps;
         if (best_cost < 0 || cost < best_cost) {

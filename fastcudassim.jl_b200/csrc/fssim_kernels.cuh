@@ -7,18 +7,20 @@
 // Decomposition.  A CTA owns one channel c of one image n, a band of T output
 // rows [h0, h0+T) along the contiguous height axis, and a segment of output
 // columns [w0, w0+L) along the width axis.  It streams along the width axis in
-// steps of S = 8 columns:
+// steps of S columns:
 //
-//   loader  global (C,H,W,N) -> smem staging, one step ahead through registers
-//           (the element type is converted here: Float32, Float16, N0f8)
+//   loader  global (C,H,W,N) -> shared staging, two steps ahead with cp.async
+//           (Float32 I/O) or one step ahead through registers with an in-kernel
+//           conversion (Float16, N0f8 inputs; Float16 / Float64 gradients)
 //   F1      h-direction 11-tap Gaussian of the 4 moment images x, y, x^2+y^2, xy
-//           (each thread: 8 consecutive rows of one column; taps from smem)
+//           (each thread: V = 8 consecutive rows of one column; taps from smem)
 //   F2      w-direction 11-tap Gaussian (each thread: one row; the 10 previous
 //           columns stay in registers, so no column is ever recomputed inside a
 //           segment), then the SSIM map and, for gradients, the three partial
-//           derivatives dS/dM, dS/dQ, dS/dP at that pixel (zero outside the image)
+//           derivatives dS/dQ, dS/dM, dS/dP at that pixel (zero outside the image),
+//           pre-scaled by +-1/N so the backward pass needs no final multiply
 //   B1, B2  the same two passes over the partial-derivative images, then the
-//           combine 2x*K(dQ) + K(dM) + y*K(dP), scaled by +-1/N (or +-0.5/N)
+//           combine x*K(2 dQ) + K(dM) + y*K(dP)
 //
 // With gradients the forward stages run on the band plus a 5-row halo (the
 // backward correlation needs partials there); the width halo costs nothing but
@@ -28,6 +30,7 @@
 // Only four moment images are convolved, not the reference's five: the SSIM map
 // needs the two variances only through their sum, so E[x^2] and E[y^2] are
 // convolved together as E[x^2 + y^2] (t = E[x^2+y^2] - mx^2 - my^2 + C2).
+// Pairs of moments share one packed FP32x2 FMA (FFMA2) per tap.
 //
 // Per-image sums: each CTA writes one double to the workspace; the last CTA of
 // an image (atomic counter) adds them in a fixed order, divides by N and applies
@@ -42,11 +45,8 @@ namespace fssim {
 
 constexpr int RAD = 5;              // Gaussian radius (src/core.jl:41)
 constexpr int TAPS = 2 * RAD + 1;   // 11
-constexpr int S = 8;                // columns per streaming step
 constexpr int V = 8;                // rows per thread in the h-direction passes
 constexpr int HIST = 2 * RAD;       // columns of history kept in registers
-constexpr int SP = S + 1;           // staging row stride, in float2 (odd: conflict-free)
-constexpr int FC = S + 1;           // float4 buffer row stride, in float4 (odd: conflict-free)
 
 enum DType { DT_F32 = 0, DT_F16 = 1, DT_U8 = 2, DT_F64 = 3 };
 
@@ -128,23 +128,34 @@ __device__ __forceinline__ void cp_async_wait()
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
-// Shared-memory footprint of one CTA, in bytes (host and device agree on it).
-template <int NT, bool FUSED, bool F32IO>
-struct Smem {
+// Geometry and shared-memory footprint of one CTA (host and device agree on it).
+template <int NT, int S, bool FUSED, bool F32IO>
+struct Geo {
     static constexpr int R1 = NT;                          // moment / partial rows
     static constexpr int T = FUSED ? NT - 2 * RAD : NT;    // output rows of a band
     static constexpr int R2 = R1 + 2 * RAD;                // input rows
-    static constexpr int NRUNB = (T + V - 1) / V;          // runs of the B1 pass
+    static constexpr int LAG = FUSED ? 2 * RAD : RAD;      // input row/column offset of the stream
+    static constexpr int SP = S + 1;                       // staging row stride (float2), odd
+    static constexpr int FC = S + 1;                       // float4 row stride, odd: conflict-free
+    static constexpr int NRUN1 = R1 / V;                   // F1 runs per column
+    static constexpr int IT1 = S * NRUN1 / NT;             // F1 items per thread
+    static constexpr int NRUNB = (T + V - 1) / V;          // B1 runs per column
+    static constexpr int ITB = (S * NRUNB + NT - 1) / NT;  // B1 items per thread (last round partial)
     static constexpr int QROWS = NRUNB * V + 2 * RAD;      // partial rows incl. zero padding
-    static constexpr int stage_one = R2 * SP * 8;                // one staging buffer
-    static constexpr int stage_bytes = (F32IO ? 2 : 1) * stage_one;   // cp.async path double-buffers
+    static constexpr int LROWS = (R2 + NT - 1) / NT;       // staging rows per thread (cp.async loader)
+    static constexpr int NLOAD = (R2 * S + NT - 1) / NT;   // staged elements per thread (register loader)
+    static constexpr int stage_one = R2 * SP * 8;
+    static constexpr int stage_bytes = (F32IO ? 2 : 1) * stage_one;
     static constexpr int f1_bytes = R1 * FC * 16;
     static constexpr int qmp_bytes = FUSED ? QROWS * FC * 16 : 0;
     static constexpr int b1_bytes = FUSED ? NT * FC * 16 : 0;
     static constexpr int lut_bytes = F32IO ? 0 : 256 * 4;
     static constexpr int red_bytes = (NT / 32 + 2) * 8;
     static constexpr int total = stage_bytes + f1_bytes + qmp_bytes + b1_bytes + lut_bytes + red_bytes;
-    static_assert(stage_bytes % 16 == 0, "staging must keep 16-byte alignment");
+    static_assert(R1 % V == 0 && NT % 32 == 0, "band geometry");
+    static_assert((S * NRUN1) % NT == 0, "F1 items must divide evenly over the CTA");
+    static_assert(NRUNB * V <= NT, "B1 rows must fit the B2 buffer");
+    static_assert(stage_one % 16 == 0, "staging must keep 16-byte alignment");
 };
 
 // Reduce a per-thread double over the CTA in a fixed order; result valid in thread 0.
@@ -195,28 +206,21 @@ __device__ __forceinline__ void finish_image(const Params& p, int n, int local_c
 // F32IO: both inputs and the gradient are Float32 - loads go straight to shared
 // memory with cp.async (double-buffered, two steps ahead) and no conversion;
 // otherwise elements are loaded by type, converted, and staged through registers.
-template <int NT, bool FUSED, bool WANT_SSIM, bool F32IO>
+template <int NT, int S, bool FUSED, bool WANT_SSIM, bool F32IO>
 __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
 {
-    using SM = Smem<NT, FUSED, F32IO>;
-    constexpr int R1 = SM::R1;
-    constexpr int T = SM::T;
-    constexpr int R2 = SM::R2;
-    constexpr int NRUNB = SM::NRUNB;
-    constexpr int QROWS = SM::QROWS;
-    constexpr int LAG = FUSED ? 2 * RAD : RAD;      // input column/row offset of the stream
-    constexpr int NLOAD = (R2 * S + NT - 1) / NT;  // staged elements per thread per step
-    static_assert(R1 % V == 0 && NT % 32 == 0, "band geometry");
-    static_assert(R1 / V * S == NT, "F1 runs must cover the CTA exactly");
+    using G = Geo<NT, S, FUSED, F32IO>;
+    constexpr int R1 = G::R1, T = G::T, R2 = G::R2, LAG = G::LAG;
+    constexpr int SP = G::SP, FC = G::FC;
+    constexpr int NRUNB = G::NRUNB, QROWS = G::QROWS;
 
     extern __shared__ __align__(16) unsigned char smem_raw[];
     float2* stage = reinterpret_cast<float2*>(smem_raw);
-    float4* f1buf = reinterpret_cast<float4*>(smem_raw + SM::stage_bytes);
-    float4* qmp = reinterpret_cast<float4*>(smem_raw + SM::stage_bytes + SM::f1_bytes);
-    float4* b1buf = reinterpret_cast<float4*>(smem_raw + SM::stage_bytes + SM::f1_bytes + SM::qmp_bytes);
-    float* lut = reinterpret_cast<float*>(smem_raw + SM::stage_bytes + SM::f1_bytes + SM::qmp_bytes +
-                                          SM::b1_bytes);
-    double* red = reinterpret_cast<double*>(smem_raw + SM::total - SM::red_bytes);
+    float4* f1buf = reinterpret_cast<float4*>(smem_raw + G::stage_bytes);
+    float4* qmp = reinterpret_cast<float4*>(smem_raw + G::stage_bytes + G::f1_bytes);
+    float4* b1buf = reinterpret_cast<float4*>(smem_raw + G::stage_bytes + G::f1_bytes + G::qmp_bytes);
+    float* lut = reinterpret_cast<float*>(smem_raw + G::stage_bytes + G::f1_bytes + G::qmp_bytes + G::b1_bytes);
+    double* red = reinterpret_cast<double*>(smem_raw + G::total - G::red_bytes);
 
     const int tid = threadIdx.x;
     int64_t blk = blockIdx.x;
@@ -227,40 +231,64 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
     const int band = static_cast<int>(blk % p.nb);
     const int n = static_cast<int>(blk / p.nb);
     const int C = p.C, H = p.H, W = p.W;
+    const int64_t CH = static_cast<int64_t>(C) * H;   // element stride of one column
     const int h0 = band * T;
     const int w0 = seg * p.L;
     const int wend = min(w0 + p.L, W);
     const int Lc = wend - w0;
     const int64_t ibase = static_cast<int64_t>(n) * p.img_elems + c;
-    const int ns = FUSED ? (Lc + 12 + S - 1) / S + 1 : (Lc + 2 + S - 1) / S + 1;
+    // Steps: the last owned output column (stream coordinate Lc-1+2*LAG-... ) must come
+    // out of the final step: ns = ceil((Lc + 2*LAG - S) / S) + 1.
+    const int ns = (Lc + 2 * LAG - 1) / S + 1;
+
+    // Gaussian weights as (k, k) pairs for the packed FMAs.
+    float2 KP[RAD + 1];
+#pragma unroll
+    for (int i = 0; i <= RAD; ++i) KP[i] = make_float2(p.kh[i], p.kh[i]);
+#define FSSIM_K2(tap) KP[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
+#define FSSIM_K1(tap) p.kh[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
 
     if (!F32IO)
         for (int i = tid; i < 256; i += NT) lut[i] = __fdiv_rn(static_cast<float>(i), 255.0f);
     if (FUSED)
         for (int e = tid; e < (QROWS - R1) * FC; e += NT) qmp[R1 * FC + e] = make_float4(0.f, 0.f, 0.f, 0.f);
 
-    // ---------------- loader: one step of S columns x R2 rows ----------------
-    auto issue_async = [&](int k, float2* buf) {
+    // ---------------- loaders: one step = S columns x R2 rows ----------------
+    // cp.async loader (F32IO): thread `tid` owns staging rows tid, tid+NT, ...
+    // and walks the S columns of the step; lanes cover consecutive rows.
+    int64_t lrow_base[G::LROWS];
+    bool lrow_ok[G::LROWS];
 #pragma unroll
-        for (int u = 0; u < NLOAD; ++u) {
-            const int e = tid + NT * u;
-            if (e < R2 * S) {
-                const int i = e % R2, j = e / R2;
-                const int hr = h0 - LAG + i;
-                const int wc = w0 - LAG + k * S + j;
-                const bool ok = k < ns && hr >= 0 && hr < H && wc >= 0 && wc < W;
-                const int64_t g = ok ? ibase + static_cast<int64_t>(C) * (hr + static_cast<int64_t>(H) * wc) : 0;
-                float2* d = buf + i * SP + j;
-                cp_async4(&d->x, reinterpret_cast<const float*>(p.x) + g, ok);
-                cp_async4(&d->y, reinterpret_cast<const float*>(p.y) + g, ok);
+    for (int r = 0; r < G::LROWS; ++r) {
+        const int i = tid + NT * r;
+        const int hr = h0 - LAG + i;
+        lrow_ok[r] = i < R2 && hr >= 0 && hr < H;
+        lrow_base[r] = ibase + static_cast<int64_t>(C) * hr;
+    }
+    auto issue_async = [&](int k, float2* buf) {
+        const int cb = w0 - LAG + k * S;   // image column of staging column 0
+#pragma unroll
+        for (int r = 0; r < G::LROWS; ++r) {
+            const int i = tid + NT * r;
+            if (i < R2) {
+#pragma unroll
+                for (int j = 0; j < S; ++j) {
+                    const int wc = cb + j;
+                    const bool ok = lrow_ok[r] && k < ns && static_cast<unsigned>(wc) < static_cast<unsigned>(W);
+                    const int64_t g = ok ? lrow_base[r] + CH * wc : 0;
+                    float2* d = buf + i * SP + j;
+                    cp_async4(&d->x, reinterpret_cast<const float*>(p.x) + g, ok);
+                    cp_async4(&d->y, reinterpret_cast<const float*>(p.y) + g, ok);
+                }
             }
         }
         cp_async_commit();
     };
-    uint32_t rx[F32IO ? 1 : NLOAD], ry[F32IO ? 1 : NLOAD];
+    // register loader (other dtypes): element e = tid + NT*u of the step.
+    uint32_t rx[F32IO ? 1 : G::NLOAD], ry[F32IO ? 1 : G::NLOAD];
     auto issue_loads = [&](int k) {
 #pragma unroll
-        for (int u = 0; u < (F32IO ? 0 : NLOAD); ++u) {
+        for (int u = 0; u < (F32IO ? 0 : G::NLOAD); ++u) {
             const int e = tid + NT * u;
             rx[u] = 0u;
             ry[u] = 0u;
@@ -269,7 +297,7 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
                 const int hr = h0 - LAG + i;
                 const int wc = w0 - LAG + k * S + j;
                 if (k < ns && hr >= 0 && hr < H && wc >= 0 && wc < W) {
-                    const int64_t g = ibase + static_cast<int64_t>(C) * (hr + static_cast<int64_t>(H) * wc);
+                    const int64_t g = ibase + static_cast<int64_t>(C) * hr + CH * wc;
                     rx[u] = ld_raw(p.x, p.xdt, g);
                     ry[u] = ld_raw(p.y, p.ydt, g);
                 }
@@ -278,7 +306,7 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
     };
     auto store_stage = [&]() {
 #pragma unroll
-        for (int u = 0; u < (F32IO ? 0 : NLOAD); ++u) {
+        for (int u = 0; u < (F32IO ? 0 : G::NLOAD); ++u) {
             const int e = tid + NT * u;
             if (e < R2 * S) {
                 const int i = e % R2, j = e / R2;
@@ -289,7 +317,7 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
 
     if (F32IO) {
         issue_async(0, stage);
-        issue_async(1, stage + SM::R2 * SP);
+        issue_async(1, stage + R2 * SP);
         cp_async_wait<1>();
     } else {
         issue_loads(0);
@@ -299,18 +327,16 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
     }
     __syncthreads();
 
-    // F1 / B1 role: column j1 of the step, run q1 of V consecutive rows.
-    const int j1 = tid & (S - 1);
-    const int q1 = tid >> 3;
     // F2 role: row `tid` of the R1 rows; B2 role: output row `tid` of the band.
     const int hr2 = h0 - LAG + RAD + tid;               // image row of the F2 row
     const bool row_in = hr2 >= 0 && hr2 < H;
     const bool row_owned = row_in && (FUSED ? (tid >= RAD && tid < RAD + T) : true);
     const int hg = h0 + tid;                            // image row of the B2 row
     const bool grow_owned = FUSED && tid < T && hg < H;
+    const int64_t grow_base = ibase + static_cast<int64_t>(C) * (grow_owned ? hg : 0);
 
     float2 hA[HIST], hB[HIST];          // (mx, my), (E[x^2+y^2], E[xy]) history of F1 columns
-    float2 gQM[HIST];                   // (dQ, dM) history of B1 columns
+    float2 gQM[HIST];                   // (2 dQ, dM) history of B1 columns
     float gP[HIST];                     // dP history of B1 columns
 #pragma unroll
     for (int m = 0; m < HIST; ++m) {
@@ -321,34 +347,39 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
     }
     double tsum = 0.0;
 
+#pragma unroll 1
     for (int k = 0; k < ns; ++k) {
         // ---------------- F1: h-direction pass of the 4 moment images ----------------
-        const float2* st = F32IO ? stage + (k & 1) * (SM::R2 * SP) : stage;
         {
-            float2 aA[V], aB[V];
-#pragma unroll
-            for (int o = 0; o < V; ++o) {
-                aA[o] = make_float2(0.f, 0.f);
-                aB[o] = make_float2(0.f, 0.f);
-            }
-#pragma unroll
-            for (int i = 0; i < V + 2 * RAD; ++i) {
-                const float2 xy = st[(V * q1 + i) * SP + j1];
-                const float2 pr = __fmul2_rn(make_float2(xy.x, xy.x), xy);        // (x^2, xy)
-                const float2 sb = make_float2(fmaf(xy.y, xy.y, pr.x), pr.y);      // (x^2+y^2, xy)
+            const float2* st = F32IO ? stage + (k & 1) * (R2 * SP) : stage;
+#pragma unroll 1
+            for (int it = 0; it < G::IT1; ++it) {
+                const int item = tid + NT * it;
+                const int j1 = item % S, q1 = item / S;
+                float2 aA[V], aB[V];
 #pragma unroll
                 for (int o = 0; o < V; ++o) {
-                    const int tap = i - o;
-                    if (tap >= 0 && tap < TAPS) {
-                        const float2 kk = make_float2(p.kh[tap <= RAD ? tap : 2 * RAD - tap], p.kh[tap <= RAD ? tap : 2 * RAD - tap]);
-                        aA[o] = __ffma2_rn(xy, kk, aA[o]);
-                        aB[o] = __ffma2_rn(sb, kk, aB[o]);
+                    aA[o] = make_float2(0.f, 0.f);
+                    aB[o] = make_float2(0.f, 0.f);
+                }
+#pragma unroll
+                for (int i = 0; i < V + 2 * RAD; ++i) {
+                    const float2 xy = st[(V * q1 + i) * SP + j1];
+                    const float2 pr = __fmul2_rn(make_float2(xy.x, xy.x), xy);   // (x^2, xy)
+                    const float2 sb = make_float2(fmaf(xy.y, xy.y, pr.x), pr.y); // (x^2+y^2, xy)
+#pragma unroll
+                    for (int o = 0; o < V; ++o) {
+                        const int tap = i - o;
+                        if (tap >= 0 && tap < TAPS) {
+                            aA[o] = __ffma2_rn(xy, FSSIM_K2(tap), aA[o]);
+                            aB[o] = __ffma2_rn(sb, FSSIM_K2(tap), aB[o]);
+                        }
                     }
                 }
-            }
 #pragma unroll
-            for (int o = 0; o < V; ++o)
-                f1buf[(V * q1 + o) * FC + j1] = make_float4(aA[o].x, aA[o].y, aB[o].x, aB[o].y);
+                for (int o = 0; o < V; ++o)
+                    f1buf[(V * q1 + o) * FC + j1] = make_float4(aA[o].x, aA[o].y, aB[o].x, aB[o].y);
+            }
         }
         __syncthreads();
 
@@ -356,12 +387,13 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
         {
             // the staging buffer F1 just read is free: refill it two steps ahead
             if (F32IO) {
-                issue_async(k + 2, stage + (k & 1) * (SM::R2 * SP));
+                issue_async(k + 2, stage + (k & 1) * (R2 * SP));
             } else {
                 store_stage();       // step k+1, held in registers since the last step
                 issue_loads(k + 2);
             }
 
+            const int wcb = w0 - LAG + k * S - RAD;   // image column of output o = 0
             float2 nA[S], nB[S];
             float ssum = 0.f;
 #pragma unroll
@@ -377,9 +409,8 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
                     const int m = o + tap;
                     const float2 wa = (m < HIST) ? hA[m] : nA[m - HIST];
                     const float2 wb = (m < HIST) ? hB[m] : nB[m - HIST];
-                    const float2 kk = make_float2(p.kh[tap <= RAD ? tap : 2 * RAD - tap], p.kh[tap <= RAD ? tap : 2 * RAD - tap]);
-                    a = __ffma2_rn(wa, kk, a);
-                    b = __ffma2_rn(wb, kk, b);
+                    a = __ffma2_rn(wa, FSSIM_K2(tap), a);
+                    b = __ffma2_rn(wb, FSSIM_K2(tap), b);
                 }
                 const float mx = a.x, my = a.y, qs = b.x, pxy = b.y;
                 const float2 sq = __fmul2_rn(a, a);                  // (mx^2, my^2)
@@ -387,23 +418,25 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
                 const float sumsq = sq.x + sq.y;
                 const float z = sumsq + p.C1;                        // mx^2 + my^2 + C1
                 const float t = (qs - sumsq) + p.C2;                 // vx + vy + C2
-                const float ax = fmaf(2.f, mxy, p.C1);               // 2 mx my + C1
-                const float by = fmaf(2.f, pxy - mxy, p.C2);         // 2 cov + C2
+                const float2 ab = __ffma2_rn(make_float2(2.f, 2.f), make_float2(mxy, pxy - mxy),
+                                             make_float2(p.C1, p.C2));   // (2 mx my + C1, 2 cov + C2)
+                const float ax = ab.x, by = ab.y;
                 const float inv = rcp_approx(z * t);
                 const float s = (ax * by) * inv;
-                const int wc = w0 - LAG + k * S - RAD + o;           // image column of this pixel
+                const int wc = wcb + o;                              // image column of this pixel
                 if (WANT_SSIM) {
-                    if (row_owned && wc >= w0 && wc < wend) ssum += s;
+                    if (row_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc)) ssum += s;
                 }
                 if (FUSED) {
                     // dS/dQ = -s/t, dS/dM = 2/(zt) ((by-ax) my + s (z-t) mx), dS/dP = 2 ax/(zt)
-                    // (src/core.jl:384-388; docs/src/math.md, "Gradients")
-                    const float inv2 = 2.f * inv;
-                    const float dq = -(s * z) * inv;
+                    // (src/core.jl:384-388; docs/src/math.md, "Gradients"), times +-1/N and
+                    // zero outside the image; dQ is stored doubled (it is used as 2x dQ).
+                    const bool in_img = row_in && static_cast<unsigned>(wc) < static_cast<unsigned>(W);
+                    const float inv2 = in_img ? 2.f * p.gscale * inv : 0.f;
+                    const float dq2 = -(s * z) * inv2;             // 2 dQ = -2 s/t = -2 s z / (zt)
                     const float dm = inv2 * fmaf(by - ax, my, (s * (z - t)) * mx);
                     const float dp = ax * inv2;
-                    const bool in_img = row_in && wc >= 0 && wc < W;
-                    qmp[tid * FC + o] = in_img ? make_float4(dq, dm, dp, 0.f) : make_float4(0.f, 0.f, 0.f, 0.f);
+                    qmp[tid * FC + o] = make_float4(dq2, dm, dp, 0.f);
                 }
             }
             if (WANT_SSIM) tsum += static_cast<double>(ssum);
@@ -419,35 +452,41 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
 
         if (FUSED) {
             // ---------------- B1: h-direction pass of the partials ----------------
-            if (q1 < NRUNB) {
-                float2 aQM[V];
-                float aP[V];
-#pragma unroll
-                for (int o = 0; o < V; ++o) {
-                    aQM[o] = make_float2(0.f, 0.f);
-                    aP[o] = 0.f;
-                }
-#pragma unroll
-                for (int i = 0; i < V + 2 * RAD; ++i) {
-                    const float4 v = qmp[(V * q1 + i) * FC + j1];
-                    const float2 qm = make_float2(v.x, v.y);
+#pragma unroll 1
+            for (int it = 0; it < G::ITB; ++it) {
+                const int item = tid + NT * it;
+                const int j1 = item % S, q1 = item / S;
+                if (q1 < NRUNB) {
+                    float2 aQM[V];
+                    float aP[V];
 #pragma unroll
                     for (int o = 0; o < V; ++o) {
-                        const int tap = i - o;
-                        if (tap >= 0 && tap < TAPS) {
-                            aQM[o] = __ffma2_rn(qm, make_float2(p.kh[tap <= RAD ? tap : 2 * RAD - tap], p.kh[tap <= RAD ? tap : 2 * RAD - tap]), aQM[o]);
-                            aP[o] = fmaf(v.z, p.kh[tap <= RAD ? tap : 2 * RAD - tap], aP[o]);
+                        aQM[o] = make_float2(0.f, 0.f);
+                        aP[o] = 0.f;
+                    }
+#pragma unroll
+                    for (int i = 0; i < V + 2 * RAD; ++i) {
+                        const float4 v = qmp[(V * q1 + i) * FC + j1];
+                        const float2 qm = make_float2(v.x, v.y);
+#pragma unroll
+                        for (int o = 0; o < V; ++o) {
+                            const int tap = i - o;
+                            if (tap >= 0 && tap < TAPS) {
+                                aQM[o] = __ffma2_rn(qm, FSSIM_K2(tap), aQM[o]);
+                                aP[o] = fmaf(v.z, FSSIM_K1(tap), aP[o]);
+                            }
                         }
                     }
-                }
 #pragma unroll
-                for (int o = 0; o < V; ++o)
-                    b1buf[(V * q1 + o) * FC + j1] = make_float4(aQM[o].x, aQM[o].y, aP[o], 0.f);
+                    for (int o = 0; o < V; ++o)
+                        b1buf[(V * q1 + o) * FC + j1] = make_float4(aQM[o].x, aQM[o].y, aP[o], 0.f);
+                }
             }
             __syncthreads();
 
             // ---------------- B2: w-direction pass and the combine ----------------
             {
+                const int wcg = w0 - LAG + k * S - 2 * RAD;   // image column of output o = 0
                 float2 nQM[S];
                 float nP[S];
 #pragma unroll
@@ -464,22 +503,24 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
                         const int m = o + tap;
                         const float2 wq = (m < HIST) ? gQM[m] : nQM[m - HIST];
                         const float wp = (m < HIST) ? gP[m] : nP[m - HIST];
-                        a = __ffma2_rn(wq, make_float2(p.kh[tap <= RAD ? tap : 2 * RAD - tap], p.kh[tap <= RAD ? tap : 2 * RAD - tap]), a);
-                        bp = fmaf(wp, p.kh[tap <= RAD ? tap : 2 * RAD - tap], bp);
+                        a = __ffma2_rn(wq, FSSIM_K2(tap), a);
+                        bp = fmaf(wp, FSSIM_K1(tap), bp);
                     }
-                    const int wc = w0 - LAG + k * S - 2 * RAD + o;
-                    if (grow_owned && wc >= w0 && wc < wend) {
-                        const int64_t g = ibase + static_cast<int64_t>(C) * (hg + static_cast<int64_t>(H) * wc);
-                        float xv, yv;
-                        if (F32IO) {
-                            xv = __ldg(reinterpret_cast<const float*>(p.x) + g);
-                            yv = __ldg(reinterpret_cast<const float*>(p.y) + g);
-                        } else {
-                            xv = cvt_raw(ld_raw(p.x, p.xdt, g), p.xdt, lut);
-                            yv = cvt_raw(ld_raw(p.y, p.ydt, g), p.ydt, lut);
-                        }
-                        // src/core.jl:773-782: (2 x K(dQ) + K(dM) + y K(dP)) * N_inv
-                        const float gv = fmaf(yv, bp, fmaf(2.f * xv, a.x, a.y)) * p.gscale;
+                    const int wc = wcg + o;
+                    const bool own = grow_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc);
+                    // loads are unconditional (a valid address when not owned); only the store is predicated
+                    const int64_t g = grow_base + CH * (own ? wc : 0);
+                    float xv, yv;
+                    if (F32IO) {
+                        xv = __ldg(reinterpret_cast<const float*>(p.x) + g);
+                        yv = __ldg(reinterpret_cast<const float*>(p.y) + g);
+                    } else {
+                        xv = cvt_raw(ld_raw(p.x, p.xdt, g), p.xdt, lut);
+                        yv = cvt_raw(ld_raw(p.y, p.ydt, g), p.ydt, lut);
+                    }
+                    // src/core.jl:773-782: (2 x K(dQ) + K(dM) + y K(dP)) * N_inv (N_inv folded upstream)
+                    const float gv = fmaf(yv, bp, fmaf(xv, a.x, a.y));
+                    if (own) {
                         if (F32IO) reinterpret_cast<float*>(p.grad)[g] = gv;
                         else st_grad(p.grad, p.gdt, g, gv);
                     }
@@ -496,6 +537,8 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
             // before the B1 barrier) and b1buf only after two more barriers.
         }
     }
+#undef FSSIM_K2
+#undef FSSIM_K1
 
     if (WANT_SSIM) {
         const int local_cta = (band * p.nseg + seg) * p.C + c;
