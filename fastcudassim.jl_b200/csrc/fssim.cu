@@ -62,8 +62,9 @@ const Weights& weights()
 struct KInfo {
     const void* fn;
     int smem;
-    int nt;
-    int s;
+    int nt;        // band geometry parameter (rows of moments per band)
+    int s;         // columns per streaming step
+    int threads;   // CTA size
 };
 
 // Kernel variants: band height NT (threads), step width S (columns), with or
@@ -72,7 +73,14 @@ template <int NT, int S, bool F, bool WS, bool IO>
 KInfo kinfo()
 {
     return KInfo{reinterpret_cast<const void*>(&fssim::band_kernel<NT, S, F, WS, IO>),
-                 fssim::Geo<NT, S, F, IO>::total, NT, S};
+                 fssim::Geo<NT, S, F, IO>::total, NT, S, NT};
+}
+
+template <int NT, bool WS>
+KInfo pinfo()
+{
+    return KInfo{reinterpret_cast<const void*>(&fssim::pipe_kernel<NT, WS>), fssim::PGeo<NT>::total, NT,
+                 fssim::PGeo<NT>::S, 2 * NT};
 }
 
 template <int S, bool IO>
@@ -94,10 +102,15 @@ KInfo kernel_info_s(int nt, bool fused, bool want_ssim)
 // Float32 I/O streams 16 columns per step (cp.async staging); the converting
 // kernels stream 8 (their staging goes through registers).
 #ifndef FSSIM_F32_STEP
-#define FSSIM_F32_STEP 16
+#define FSSIM_F32_STEP 8
 #endif
+// SSIM + gradient with Float32 I/O runs the two-group pipelined kernel.
 KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io)
 {
+    if (f32io && fused) {   // (the caller guarantees C*H*W < 2^31: 32-bit in-image offsets)
+        if (nt == 64) return want_ssim ? pinfo<64, true>() : pinfo<64, false>();
+        return want_ssim ? pinfo<96, true>() : pinfo<96, false>();
+    }
     return f32io ? kernel_info_s<FSSIM_F32_STEP, true>(nt, fused, want_ssim)
                  : kernel_info_s<8, false>(nt, fused, want_ssim);
 }
@@ -126,7 +139,7 @@ int device_facts(const KInfo& ki, int* sms, int* occ)
         e = cudaFuncSetAttribute(ki.fn, cudaFuncAttributeMaxDynamicSharedMemorySize, ki.smem);
         if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "cudaFuncSetAttribute: %s", cudaGetErrorString(e));
         int o = 0;
-        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, ki.fn, ki.nt, ki.smem);
+        e = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&o, ki.fn, ki.threads, ki.smem);
         if (e != cudaSuccess)
             return fail(FSSIM_ERR_CUDA, "cudaOccupancyMaxActiveBlocksPerMultiprocessor: %s", cudaGetErrorString(e));
         if (o < 1) o = 1;
@@ -300,7 +313,7 @@ int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimg
     if (!want_ssim && !fused) return ok();   // nothing requested
 
     const bool f32io = imgs1_dtype == FSSIM_FLOAT32 && imgs2_dtype == FSSIM_FLOAT32 &&
-                       (!fused || grad_dtype == FSSIM_FLOAT32);
+                       (!fused || grad_dtype == FSSIM_FLOAT32) && c * h * w < (int64_t(1) << 31);
     Cfg g;
     st = configure(c, h, w, n, flags, f32io, &g);
     if (st != FSSIM_OK) return st;
@@ -345,7 +358,7 @@ int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimg
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     void* args[] = {&p};
-    cudaError_t e = cudaLaunchKernel(g.ki.fn, dim3(static_cast<unsigned>(g.grid)), dim3(g.nt), args, g.ki.smem, s);
+    cudaError_t e = cudaLaunchKernel(g.ki.fn, dim3(static_cast<unsigned>(g.grid)), dim3(g.ki.threads), args, g.ki.smem, s);
     if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
     return ok();
 }

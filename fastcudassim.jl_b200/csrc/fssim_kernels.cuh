@@ -547,3 +547,346 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
 }
 
 }  // namespace fssim
+
+namespace fssim {
+
+// ---------------------------------------------------------------------------
+// Two-group pipelined kernel: SSIM + gradient, Float32 inputs and gradient.
+//
+// The same streaming decomposition as band_kernel, but the CTA is split into
+// two warp groups of NT threads that work on different steps at once:
+//
+//   group A (threads 0..NT-1):    cp.async loads (inputs, and the x/y values B2
+//                                 needs), F1(t), B1(t-2)
+//   group B (threads NT..2NT-1):  F2(t-1) + SSIM map + partials, B2(t-3)
+//
+// Every stage reads only what the other group wrote in the previous slot, so a
+// single __syncthreads() per slot orders everything; the buffers passed between
+// the groups are double-buffered by step parity.
+//
+// Group B keeps, per row, the last 10 columns of the F1 output and of the B1
+// output in registers (shifted by 8 columns per slot).  Both loops stay
+// compact: unrolling group B over 5 slots (to index the histories as rings at
+// compile time) was measured slower - the larger body misses the instruction
+// cache.
+// ---------------------------------------------------------------------------
+template <int NT>
+struct PGeo {
+    static constexpr int S = 8;
+    static constexpr int R1 = NT, T = NT - 2 * RAD, R2 = NT + 2 * RAD, LAG = 2 * RAD;
+    static constexpr int SP = S + 1, FC = S + 1;
+    static constexpr int NRUNB = (T + V - 1) / V;
+    static constexpr int QROWS = NRUNB * V + 2 * RAD;
+    static constexpr int LROWS = (R2 + NT - 1) / NT;
+    static constexpr int LATENCY = 3;    // slots from F1(k) to B2(k)
+    static constexpr int stage_one = R2 * SP * 8;
+    static constexpr int f1_one = R1 * FC * 16;
+    static constexpr int qmp_one = QROWS * FC * 16;
+    static constexpr int b1_one = NT * FC * 16;
+    static constexpr int xy_one = NT * SP * 8;
+    static constexpr int red_bytes = (2 * NT / 32 + 2) * 8;
+    static constexpr int off_stage = 0;
+    static constexpr int off_f1 = off_stage + 2 * stage_one;
+    static constexpr int off_qmp = off_f1 + 2 * f1_one;
+    static constexpr int off_b1 = off_qmp + 2 * qmp_one;
+    static constexpr int off_xy = off_b1 + 2 * b1_one;
+    static constexpr int off_red = off_xy + 2 * xy_one;
+    static constexpr int total = off_red + red_bytes;
+    static_assert(R1 % V == 0 && NT % 32 == 0 && S * (R1 / V) == NT, "F1 items = one per thread");
+    static_assert(S * NRUNB <= NT, "B1 items fit one round");
+    static_assert(stage_one % 16 == 0 && xy_one % 16 == 0, "16-byte alignment of the buffers");
+};
+
+template <int NT, bool WANT_SSIM>
+__global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Params p)
+{
+    using G = PGeo<NT>;
+    constexpr int S = G::S, R1 = G::R1, T = G::T, R2 = G::R2, LAG = G::LAG;
+    constexpr int SP = G::SP, FC = G::FC, NRUNB = G::NRUNB, QROWS = G::QROWS;
+
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float2* stage = reinterpret_cast<float2*>(smem_raw + G::off_stage);
+    float4* f1buf = reinterpret_cast<float4*>(smem_raw + G::off_f1);
+    float4* qmp = reinterpret_cast<float4*>(smem_raw + G::off_qmp);
+    float4* b1buf = reinterpret_cast<float4*>(smem_raw + G::off_b1);
+    float2* xyb = reinterpret_cast<float2*>(smem_raw + G::off_xy);
+    double* red = reinterpret_cast<double*>(smem_raw + G::off_red);
+    constexpr int STG = R2 * SP, F1N = R1 * FC, QN = QROWS * FC, B1N = NT * FC, XYN = NT * SP;
+
+    const int tid = threadIdx.x;
+    const bool groupA = tid < NT;
+    int64_t blk = blockIdx.x;
+    const int c = static_cast<int>(blk % p.C);
+    blk /= p.C;
+    const int seg = static_cast<int>(blk % p.nseg);
+    blk /= p.nseg;
+    const int band = static_cast<int>(blk % p.nb);
+    const int n = static_cast<int>(blk / p.nb);
+    const int C = p.C, H = p.H, W = p.W;
+    const int h0 = band * T;
+    const int w0 = seg * p.L;
+    const int wend = min(w0 + p.L, W);
+    const int Lc = wend - w0;
+    // In-image element offsets are 32-bit (the host guarantees C*H*W < 2^31), so
+    // each address is one wide multiply-add from the image base.
+    const float* __restrict__ xg = reinterpret_cast<const float*>(p.x) + static_cast<int64_t>(n) * p.img_elems + c;
+    const float* __restrict__ yg = reinterpret_cast<const float*>(p.y) + static_cast<int64_t>(n) * p.img_elems + c;
+    float* __restrict__ gg = reinterpret_cast<float*>(p.grad) + static_cast<int64_t>(n) * p.img_elems + c;
+    const uint32_t CH32 = static_cast<uint32_t>(C) * static_cast<uint32_t>(H);
+    const int ns = (Lc + 2 * LAG - 1) / S + 1;
+    const int nslot = ns + G::LATENCY;
+
+    float2 KP[RAD + 1];
+#pragma unroll
+    for (int i = 0; i <= RAD; ++i) KP[i] = make_float2(p.kh[i], p.kh[i]);
+#define FSSIM_K2(tap) KP[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
+#define FSSIM_K1(tap) p.kh[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
+
+    for (int e = tid; e < (QROWS - R1) * FC; e += 2 * NT) {
+        qmp[R1 * FC + e] = make_float4(0.f, 0.f, 0.f, 0.f);
+        qmp[QN + R1 * FC + e] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    double tsum = 0.0;
+
+    if (groupA) {
+        // ================= group A: loads, F1, B1 =================
+        const int ta = tid;
+        const int j1 = ta & (S - 1), q1 = ta >> 3;
+        uint32_t lrow_off[G::LROWS];
+        bool lrow_ok[G::LROWS];
+#pragma unroll
+        for (int r = 0; r < G::LROWS; ++r) {
+            const int i = ta + NT * r;
+            const int hr = h0 - LAG + i;
+            lrow_ok[r] = i < R2 && hr >= 0 && hr < H;
+            lrow_off[r] = static_cast<uint32_t>(C) * static_cast<uint32_t>(lrow_ok[r] ? hr : 0);
+        }
+        const bool xyrow_ok = ta < T && h0 + ta < H;
+        const uint32_t xyrow_off = static_cast<uint32_t>(C) * static_cast<uint32_t>(xyrow_ok ? h0 + ta : 0);
+        auto issue_stage = [&](int k, float2* buf) {   // stage <- input columns of step k
+            const int cb = w0 - LAG + k * S;
+#pragma unroll
+            for (int j = 0; j < S; ++j) {
+                const int wc = cb + j;
+                const bool colok = static_cast<unsigned>(wc) < static_cast<unsigned>(W);
+                const uint32_t coloff = CH32 * static_cast<uint32_t>(colok ? wc : 0);
+#pragma unroll
+                for (int r = 0; r < G::LROWS; ++r) {
+                    const int i = ta + NT * r;
+                    if (G::LROWS == 1 || i < R2) {
+                        const bool ok = lrow_ok[r] && colok;
+                        const uint32_t off = lrow_off[r] + coloff;
+                        cp_async4(&buf[i * SP + j].x, xg + off, ok);
+                        cp_async4(&buf[i * SP + j].y, yg + off, ok);
+                    }
+                }
+            }
+        };
+        auto issue_xy = [&](int k, float2* buf) {      // xyb <- x, y at the gradient pixels of step k
+            const int cb = w0 - LAG + k * S - 2 * RAD;
+#pragma unroll
+            for (int o = 0; o < S; ++o) {
+                const int wc = cb + o;
+                const bool ok = xyrow_ok && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc);
+                const uint32_t off = xyrow_off + CH32 * static_cast<uint32_t>(ok ? wc : 0);
+                cp_async4(&buf[ta * SP + o].x, xg + off, ok);
+                cp_async4(&buf[ta * SP + o].y, yg + off, ok);
+            }
+        };
+
+        issue_stage(0, stage);
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+#pragma unroll 1
+        for (int t = 0; t < nslot; ++t) {
+            if (t + 1 < ns) issue_stage(t + 1, stage + ((t + 1) & 1) * STG);
+            if (t >= 2 && t - 2 < ns) issue_xy(t - 2, xyb + ((t + 1) & 1) * XYN);
+            cp_async_commit();
+            // -------- F1(t): h-direction pass of the 4 moment images --------
+            if (t < ns) {
+                const float2* st = stage + (t & 1) * STG;
+                float4* f1 = f1buf + (t & 1) * F1N;
+                float2 aA[V], aB[V];
+#pragma unroll
+                for (int o = 0; o < V; ++o) {
+                    aA[o] = make_float2(0.f, 0.f);
+                    aB[o] = make_float2(0.f, 0.f);
+                }
+#pragma unroll
+                for (int i = 0; i < V + 2 * RAD; ++i) {
+                    const float2 xy = st[(V * q1 + i) * SP + j1];
+                    const float2 sq = __fmul2_rn(xy, xy);                     // (x^2, y^2)
+                    const float2 sb = make_float2(sq.x + sq.y, xy.x * xy.y);  // (x^2+y^2, xy)
+#pragma unroll
+                    for (int o = 0; o < V; ++o) {
+                        const int tap = i - o;
+                        if (tap >= 0 && tap < TAPS) {
+                            aA[o] = __ffma2_rn(xy, FSSIM_K2(tap), aA[o]);
+                            aB[o] = __ffma2_rn(sb, FSSIM_K2(tap), aB[o]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int o = 0; o < V; ++o)
+                    f1[(V * q1 + o) * FC + j1] = make_float4(aA[o].x, aA[o].y, aB[o].x, aB[o].y);
+            }
+            // -------- B1(t-2): h-direction pass of the partials --------
+            if (t >= 2 && t - 2 < ns && q1 < NRUNB) {
+                const float4* qm = qmp + ((t - 2) & 1) * QN;
+                float4* b1 = b1buf + ((t - 2) & 1) * B1N;
+                float2 aQM[V];
+                float aP[V];
+#pragma unroll
+                for (int o = 0; o < V; ++o) {
+                    aQM[o] = make_float2(0.f, 0.f);
+                    aP[o] = 0.f;
+                }
+#pragma unroll
+                for (int i = 0; i < V + 2 * RAD; ++i) {
+                    const float4 v = qm[(V * q1 + i) * FC + j1];
+                    const float2 dqm = make_float2(v.x, v.y);
+#pragma unroll
+                    for (int o = 0; o < V; ++o) {
+                        const int tap = i - o;
+                        if (tap >= 0 && tap < TAPS) {
+                            aQM[o] = __ffma2_rn(dqm, FSSIM_K2(tap), aQM[o]);
+                            aP[o] = fmaf(v.z, FSSIM_K1(tap), aP[o]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int o = 0; o < V; ++o)
+                    b1[(V * q1 + o) * FC + j1] = make_float4(aQM[o].x, aQM[o].y, aP[o], 0.f);
+            }
+            cp_async_wait<0>();
+            __syncthreads();
+        }
+    } else {
+        // ================= group B: F2 + map, B2 =================
+        const int tb = tid - NT;
+        const int hr2 = h0 - LAG + RAD + tb;                 // image row of the F2 row
+        const bool row_in = hr2 >= 0 && hr2 < H;
+        const bool row_owned = row_in && tb >= RAD && tb < RAD + T;
+        const bool grow_owned = tb < T && h0 + tb < H;
+        const uint32_t grow_off = static_cast<uint32_t>(C) * static_cast<uint32_t>(grow_owned ? h0 + tb : 0);
+        // per-row histories: the last HIST columns of the F1 output and of the B1 output
+        float2 hA[HIST], hB[HIST], gQM[HIST];
+        float gP[HIST];
+#pragma unroll
+        for (int m = 0; m < HIST; ++m) {
+            hA[m] = make_float2(0.f, 0.f);
+            hB[m] = make_float2(0.f, 0.f);
+            gQM[m] = make_float2(0.f, 0.f);
+            gP[m] = 0.f;
+        }
+        __syncthreads();
+#pragma unroll 1
+        for (int t = 0; t < nslot; ++t) {
+            // -------- F2(t-1): w-direction pass, SSIM map, partials --------
+            if (t >= 1 && t - 1 < ns) {
+                const int k = t - 1;
+                const float4* f1 = f1buf + (k & 1) * F1N;
+                float4* qm = qmp + (k & 1) * QN;
+                const int wcb = w0 - LAG + k * S - RAD;
+                float2 nA[S], nB[S];
+                float ssum = 0.f;
+#pragma unroll
+                for (int o = 0; o < S; ++o) {
+                    {   // column o of this step enters the window just before its first use
+                        const float4 v = f1[tb * FC + o];
+                        nA[o] = make_float2(v.x, v.y);
+                        nB[o] = make_float2(v.z, v.w);
+                    }
+                    float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+#pragma unroll
+                    for (int tap = 0; tap < TAPS; ++tap) {
+                        const int m = o + tap;
+                        const float2 wa = (m < HIST) ? hA[m] : nA[m - HIST];
+                        const float2 wb = (m < HIST) ? hB[m] : nB[m - HIST];
+                        a = __ffma2_rn(wa, FSSIM_K2(tap), a);
+                        b = __ffma2_rn(wb, FSSIM_K2(tap), b);
+                    }
+                    const float mx = a.x, my = a.y, qs = b.x, pxy = b.y;
+                    const float2 sq = __fmul2_rn(a, a);
+                    const float mxy = mx * my;
+                    const float sumsq = sq.x + sq.y;
+                    const float z = sumsq + p.C1;                    // mx^2 + my^2 + C1
+                    const float tt = (qs - sumsq) + p.C2;            // vx + vy + C2
+                    const float ax = fmaf(2.f, mxy, p.C1);           // 2 mx my + C1
+                    const float by = fmaf(2.f, pxy - mxy, p.C2);     // 2 cov + C2
+                    const float inv = rcp_approx(z * tt);
+                    const float s = (ax * by) * inv;
+                    const int wc = wcb + o;
+                    if (WANT_SSIM) {
+                        if (row_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc)) ssum += s;
+                    }
+                    // dS/dQ = -s/t, dS/dM = 2/(zt) ((by-ax) my + s (z-t) mx), dS/dP = 2 ax/(zt)
+                    // (src/core.jl:384-388), times +-1/N, zero outside the image, dQ doubled.
+                    const bool in_img = row_in && static_cast<unsigned>(wc) < static_cast<unsigned>(W);
+                    const float inv2 = in_img ? 2.f * p.gscale * inv : 0.f;
+                    const float dq2 = -(s * z) * inv2;
+                    const float dm = inv2 * fmaf(by - ax, my, (s * (z - tt)) * mx);
+                    const float dp = ax * inv2;
+                    qm[tb * FC + o] = make_float4(dq2, dm, dp, 0.f);
+                }
+                if (WANT_SSIM) tsum += static_cast<double>(ssum);
+#pragma unroll
+                for (int m = 0; m < HIST; ++m) {
+                    const int src = m + S;
+                    hA[m] = (src < HIST) ? hA[src] : nA[src - HIST];
+                    hB[m] = (src < HIST) ? hB[src] : nB[src - HIST];
+                }
+            }
+            // -------- B2(t-3): w-direction pass and the combine --------
+            if (t >= G::LATENCY && t - G::LATENCY < ns) {
+                const int k = t - G::LATENCY;
+                const float4* b1 = b1buf + (k & 1) * B1N;
+                const float2* xy = xyb + (t & 1) * XYN;
+                const int wcg = w0 - LAG + k * S - 2 * RAD;
+                float2 nQM[S];
+                float nP[S];
+#pragma unroll
+                for (int o = 0; o < S; ++o) {
+                    {
+                        const float4 v = b1[tb * FC + o];
+                        nQM[o] = make_float2(v.x, v.y);
+                        nP[o] = v.z;
+                    }
+                    float2 a = make_float2(0.f, 0.f);
+                    float bp = 0.f;
+#pragma unroll
+                    for (int tap = 0; tap < TAPS; ++tap) {
+                        const int m = o + tap;
+                        const float2 wq = (m < HIST) ? gQM[m] : nQM[m - HIST];
+                        const float wp = (m < HIST) ? gP[m] : nP[m - HIST];
+                        a = __ffma2_rn(wq, FSSIM_K2(tap), a);
+                        bp = fmaf(wp, FSSIM_K1(tap), bp);
+                    }
+                    const int wc = wcg + o;
+                    const float2 v = xy[tb * SP + o];
+                    // src/core.jl:773-782: (2 x K(dQ) + K(dM) + y K(dP)) * N_inv (N_inv folded upstream)
+                    const float gv = fmaf(v.y, bp, fmaf(v.x, a.x, a.y));
+                    if (grow_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc))
+                        gg[grow_off + CH32 * static_cast<uint32_t>(wc)] = gv;
+                }
+#pragma unroll
+                for (int m = 0; m < HIST; ++m) {
+                    const int src = m + S;
+                    gQM[m] = (src < HIST) ? gQM[src] : nQM[src - HIST];
+                    gP[m] = (src < HIST) ? gP[src] : nP[src - HIST];
+                }
+            }
+            __syncthreads();
+        }
+    }
+#undef FSSIM_K2
+#undef FSSIM_K1
+
+    if (WANT_SSIM) {
+        const int local_cta = (band * p.nseg + seg) * p.C + c;
+        finish_image<2 * NT>(p, n, local_cta, tsum, red);
+    }
+}
+
+}  // namespace fssim
