@@ -364,3 +364,65 @@ int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimg
 }
 
 }  // extern "C"
+
+// ---------------------------------------------------------------------------
+// Allocation-free entry point.  The reduction scratch lives in this array,
+// compiled into the library; host code must not pass the array's name to a
+// kernel (on the host it only stands for the symbol), so each device's address
+// is looked up once with cudaGetSymbolAddress while that device is current.
+// ---------------------------------------------------------------------------
+static __device__ __align__(256) unsigned char g_fssim_scratch[FSSIM_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+
+std::mutex g_scratch_mu;
+std::map<int, void*> g_scratch_addr;
+
+int scratch_address(void** out)
+{
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "cudaGetDevice: %s", cudaGetErrorString(e));
+    std::lock_guard<std::mutex> lk(g_scratch_mu);
+    auto it = g_scratch_addr.find(dev);
+    if (it == g_scratch_addr.end()) {
+        void* ptr = nullptr;
+        e = cudaGetSymbolAddress(&ptr, g_fssim_scratch);
+        if (e != cudaSuccess || ptr == nullptr)
+            return fail(FSSIM_ERR_CUDA, "cudaGetSymbolAddress(scratch) on device %d: %s", dev,
+                        cudaGetErrorString(e));
+        it = g_scratch_addr.emplace(dev, ptr).first;
+    }
+    *out = it->second;
+    return FSSIM_OK;
+}
+
+}  // namespace
+
+extern "C" int fssim_fwd_bwd_noalloc(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs1,
+                                     int grad_dtype, const void* imgs1, int imgs1_dtype, const void* imgs2,
+                                     int imgs2_dtype, int64_t c, int64_t h, int64_t w, int64_t n,
+                                     uint32_t flags, void* stream)
+{
+    size_t need = 0;
+    int st = fssim_workspace_size(c, h, w, n, flags, &need);
+    if (st != FSSIM_OK) return st;
+    if (need > FSSIM_NOALLOC_SCRATCH_BYTES)
+        return fail(FSSIM_ERR_WORKSPACE,
+                    "fssim_fwd_bwd_noalloc: these sizes need %zu bytes of reduction scratch, the built-in "
+                    "scratch holds %u; call fssim_fwd_bwd with a caller-provided workspace instead",
+                    need, (unsigned)FSSIM_NOALLOC_SCRATCH_BYTES);
+    void* ws = nullptr;
+    st = scratch_address(&ws);
+    if (st != FSSIM_OK) return st;
+    if (need > 0) {
+        // The per-image counters must start at zero: a previous call that failed
+        // part-way could have left them set.  The partial sums are written before
+        // they are read and need no clearing.
+        const size_t counter_bytes = ((static_cast<size_t>(n) * sizeof(unsigned) + 255) / 256) * 256;
+        const cudaError_t e = cudaMemsetAsync(ws, 0, counter_bytes, static_cast<cudaStream_t>(stream));
+        if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "cudaMemsetAsync(scratch): %s", cudaGetErrorString(e));
+    }
+    return fssim_fwd_bwd(ssims, ssims_dtype, ssims_len, dL_dimgs1, grad_dtype, imgs1, imgs1_dtype, imgs2,
+                         imgs2_dtype, nullptr, c, h, w, n, flags, ws, FSSIM_NOALLOC_SCRATCH_BYTES, stream);
+}

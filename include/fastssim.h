@@ -110,6 +110,39 @@ int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len,
                   void* workspace, size_t workspace_bytes,
                   void* stream);
 
+/*
+ * fssim_fwd_bwd_noalloc - fssim_fwd_bwd for callers that cannot allocate device memory.
+ *
+ * No counterpart in the reference: FastCUDASSIM.jl allocates its own buffers
+ * through CUDA.jl.  Some callers of this library cannot: a plugin host that owns
+ * all device memory through its own pool and hands the plugin no allocator, or
+ * a real-time loop that forbids allocation once it has started.  They cannot
+ * provide the reduction workspace that fssim_fwd_bwd asks for, so this entry
+ * point uses a scratch array compiled into the library instead
+ * (FSSIM_NOALLOC_SCRATCH_BYTES, resident on every GPU that loads the library
+ * until the process exits).
+ *
+ * Arguments and results are those of fssim_fwd_bwd without `qmp` and the
+ * workspace.  Limits and rules:
+ *  - sizes whose workspace (fssim_workspace_size) exceeds
+ *    FSSIM_NOALLOC_SCRATCH_BYTES are rejected with FSSIM_ERR_WORKSPACE;
+ *  - no cudaMalloc, cudaFree or allocating library call is made; the scratch
+ *    counters are cleared with cudaMemsetAsync on `stream` before the launch;
+ *  - the first call on a device looks up the scratch address on that device
+ *    (cudaGetSymbolAddress); make that first call before any stream capture;
+ *  - every call on a device shares the one scratch array: calls that overlap on
+ *    the GPU (different streams, no ordering between them) race and give wrong
+ *    (D)SSIM values.  Calls on one stream are ordered and safe.
+ */
+#define FSSIM_NOALLOC_SCRATCH_BYTES (4u << 20)
+
+int fssim_fwd_bwd_noalloc(void* ssims, int ssims_dtype, int64_t ssims_len,
+                          void* dL_dimgs1, int grad_dtype,
+                          const void* imgs1, int imgs1_dtype,
+                          const void* imgs2, int imgs2_dtype,
+                          int64_t c, int64_t h, int64_t w, int64_t n,
+                          uint32_t flags, void* stream);
+
 #ifdef __cplusplus
 }
 #endif
