@@ -565,11 +565,16 @@ namespace fssim {
 // the groups are double-buffered by step parity.
 //
 // Group B keeps, per row, the last 10 columns of the F1 output and of the B1
-// output in registers (shifted by 8 columns per slot).  Both loops stay
-// compact: unrolling group B over 5 slots (to index the histories as rings at
-// compile time) was measured slower - the larger body misses the instruction
-// cache.
+// output in registers, as two 8-column blocks used in turn (its loop covers two
+// slots per iteration, so only 2 carried columns are copied per slot).
+// Unrolling further (5 slots, to index 40-column rings at compile time) was
+// measured slower: the larger body misses the instruction cache.
 // ---------------------------------------------------------------------------
+// Which group stages the x/y values B2 needs (0: group A, 1: group B).
+#ifndef FSSIM_XY_IN_B
+#define FSSIM_XY_IN_B 0
+#endif
+
 template <int NT>
 struct PGeo {
     static constexpr int S = 8;
@@ -634,7 +639,7 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
     float* __restrict__ gg = reinterpret_cast<float*>(p.grad) + static_cast<int64_t>(n) * p.img_elems + c;
     const uint32_t CH32 = static_cast<uint32_t>(C) * static_cast<uint32_t>(H);
     const int ns = (Lc + 2 * LAG - 1) / S + 1;
-    const int nslot = ns + G::LATENCY;
+    const int nslot = (ns + G::LATENCY + 1) & ~1;   // even: group B runs two slots per iteration
 
     float2 KP[RAD + 1];
 #pragma unroll
@@ -642,10 +647,15 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
 #define FSSIM_K2(tap) KP[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
 #define FSSIM_K1(tap) p.kh[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
 
-    for (int e = tid; e < (QROWS - R1) * FC; e += 2 * NT) {
-        qmp[R1 * FC + e] = make_float4(0.f, 0.f, 0.f, 0.f);
-        qmp[QN + R1 * FC + e] = make_float4(0.f, 0.f, 0.f, 0.f);
+    // Zero the hand-off buffers once: the partial rows past R1 must read as zero,
+    // and group B's first and last slots read these buffers before (after) the
+    // stream has filled them.
+    {
+        float4* z4 = f1buf;
+        const int n4 = (G::off_red - G::off_f1) / 16;   // f1buf, qmp, b1buf, xyb
+        for (int e = tid; e < n4; e += 2 * NT) z4[e] = make_float4(0.f, 0.f, 0.f, 0.f);
     }
+    __syncthreads();
     double tsum = 0.0;
 
     if (groupA) {
@@ -701,7 +711,9 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
 #pragma unroll 1
         for (int t = 0; t < nslot; ++t) {
             if (t + 1 < ns) issue_stage(t + 1, stage + ((t + 1) & 1) * STG);
+#if !FSSIM_XY_IN_B
             if (t >= 2 && t - 2 < ns) issue_xy(t - 2, xyb + ((t + 1) & 1) * XYN);
+#endif
             cp_async_commit();
             // -------- F1(t): h-direction pass of the 4 moment images --------
             if (t < ns) {
@@ -770,42 +782,68 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
         const bool row_owned = row_in && tb >= RAD && tb < RAD + T;
         const bool grow_owned = tb < T && h0 + tb < H;
         const uint32_t grow_off = static_cast<uint32_t>(C) * static_cast<uint32_t>(grow_owned ? h0 + tb : 0);
-        // per-row histories: the last HIST columns of the F1 output and of the B1 output
-        float2 hA[HIST], hB[HIST], gQM[HIST];
-        float gP[HIST];
+        // Per-row histories as two S-column blocks used in turn: the block of step
+        // k-1 ("prv"), and the block being filled by step k ("cur").  The window of
+        // step k is [two saved columns of step k-2 | prv | cur]; after the step the
+        // last two columns of prv are saved and the blocks swap roles.  The loop is
+        // unrolled by two slots so the swap is a renaming, not a copy.
+        static_assert(HIST == S + 2, "window = 2 saved columns + previous block + current block");
+        float2 A0[S], A1[S], B0[S], B1[S], TA[2], TB[2];     // F1 output: (mx, my), (E[x^2+y^2], E[xy])
+        float2 Q0[S], Q1[S], TQ[2];                         // B1 output: (2 dQ, dM)
+        float P0[S], P1[S], TP[2];                          // B1 output: dP
 #pragma unroll
-        for (int m = 0; m < HIST; ++m) {
-            hA[m] = make_float2(0.f, 0.f);
-            hB[m] = make_float2(0.f, 0.f);
-            gQM[m] = make_float2(0.f, 0.f);
-            gP[m] = 0.f;
+        for (int m = 0; m < S; ++m) {
+            A0[m] = A1[m] = B0[m] = B1[m] = Q0[m] = Q1[m] = make_float2(0.f, 0.f);
+            P0[m] = P1[m] = 0.f;
         }
-        __syncthreads();
-#pragma unroll 1
-        for (int t = 0; t < nslot; ++t) {
+        TA[0] = TA[1] = TB[0] = TB[1] = TQ[0] = TQ[1] = make_float2(0.f, 0.f);
+        TP[0] = TP[1] = 0.f;
+
+#if FSSIM_XY_IN_B
+        auto issue_xy_b = [&](int k, float2* buf) {    // xyb <- x, y at this row's gradient pixels of step k
+            const int cb = w0 - LAG + k * S - 2 * RAD;
+#pragma unroll
+            for (int o = 0; o < S; ++o) {
+                const int wc = cb + o;
+                const bool ok = grow_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc);
+                const uint32_t off = grow_off + CH32 * static_cast<uint32_t>(ok ? wc : 0);
+                cp_async4(&buf[tb * SP + o].x, xg + off, ok);
+                cp_async4(&buf[tb * SP + o].y, yg + off, ok);
+            }
+            cp_async_commit();
+        };
+#endif
+        auto bslot = [&](int t, float2(&Acur)[S], float2(&Aprv)[S], float2(&Bcur)[S], float2(&Bprv)[S],
+                         float2(&Qcur)[S], float2(&Qprv)[S], float(&Pcur)[S], float(&Pprv)[S]) {
+#if FSSIM_XY_IN_B
+            if (t >= 2 && t - 2 < ns) issue_xy_b(t - 2, xyb + ((t + 1) & 1) * XYN);
+#endif
+            // Both stages run in every slot (so the history blocks are written
+            // unconditionally and never held live twice); outside the stream they read
+            // stale or zeroed buffers, and nothing they produce there is stored or owned.
             // -------- F2(t-1): w-direction pass, SSIM map, partials --------
-            if (t >= 1 && t - 1 < ns) {
+            {
                 const int k = t - 1;
                 const float4* f1 = f1buf + (k & 1) * F1N;
                 float4* qm = qmp + (k & 1) * QN;
                 const int wcb = w0 - LAG + k * S - RAD;
-                float2 nA[S], nB[S];
                 float ssum = 0.f;
+#define FSSIM_WA(m) ((m) < 2 ? TA[(m)] : ((m) < HIST ? Aprv[(m) - 2] : Acur[(m) - HIST]))
+#define FSSIM_WB(m) ((m) < 2 ? TB[(m)] : ((m) < HIST ? Bprv[(m) - 2] : Bcur[(m) - HIST]))
 #pragma unroll
                 for (int o = 0; o < S; ++o) {
                     {   // column o of this step enters the window just before its first use
                         const float4 v = f1[tb * FC + o];
-                        nA[o] = make_float2(v.x, v.y);
-                        nB[o] = make_float2(v.z, v.w);
+                        Acur[o] = make_float2(v.x, v.y);
+                        Bcur[o] = make_float2(v.z, v.w);
                     }
-                    float2 a = make_float2(0.f, 0.f), b = make_float2(0.f, 0.f);
+                    // symmetric taps: k5 w5 + sum_t k_t (w_t + w_{10-t})
+                    float2 a = __fmul2_rn(FSSIM_WA(o + RAD), KP[RAD]);
+                    float2 b = __fmul2_rn(FSSIM_WB(o + RAD), KP[RAD]);
 #pragma unroll
-                    for (int tap = 0; tap < TAPS; ++tap) {
-                        const int m = o + tap;
-                        const float2 wa = (m < HIST) ? hA[m] : nA[m - HIST];
-                        const float2 wb = (m < HIST) ? hB[m] : nB[m - HIST];
-                        a = __ffma2_rn(wa, FSSIM_K2(tap), a);
-                        b = __ffma2_rn(wb, FSSIM_K2(tap), b);
+                    for (int tap = 0; tap < RAD; ++tap) {
+                        a = __ffma2_rn(__fadd2_rn(FSSIM_WA(o + tap), FSSIM_WA(o + 2 * RAD - tap)), KP[tap], a);
+                        b = __ffma2_rn(__fadd2_rn(FSSIM_WB(o + tap), FSSIM_WB(o + 2 * RAD - tap)), KP[tap], b);
                     }
                     const float mx = a.x, my = a.y, qs = b.x, pxy = b.y;
                     const float2 sq = __fmul2_rn(a, a);
@@ -830,38 +868,35 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
                     const float dp = ax * inv2;
                     qm[tb * FC + o] = make_float4(dq2, dm, dp, 0.f);
                 }
+#undef FSSIM_WA
+#undef FSSIM_WB
                 if (WANT_SSIM) tsum += static_cast<double>(ssum);
-#pragma unroll
-                for (int m = 0; m < HIST; ++m) {
-                    const int src = m + S;
-                    hA[m] = (src < HIST) ? hA[src] : nA[src - HIST];
-                    hB[m] = (src < HIST) ? hB[src] : nB[src - HIST];
-                }
+                TA[0] = Aprv[S - 2];
+                TA[1] = Aprv[S - 1];
+                TB[0] = Bprv[S - 2];
+                TB[1] = Bprv[S - 1];
             }
             // -------- B2(t-3): w-direction pass and the combine --------
-            if (t >= G::LATENCY && t - G::LATENCY < ns) {
+            {
                 const int k = t - G::LATENCY;
                 const float4* b1 = b1buf + (k & 1) * B1N;
                 const float2* xy = xyb + (t & 1) * XYN;
                 const int wcg = w0 - LAG + k * S - 2 * RAD;
-                float2 nQM[S];
-                float nP[S];
+#define FSSIM_WQ(m) ((m) < 2 ? TQ[(m)] : ((m) < HIST ? Qprv[(m) - 2] : Qcur[(m) - HIST]))
+#define FSSIM_WP(m) ((m) < 2 ? TP[(m)] : ((m) < HIST ? Pprv[(m) - 2] : Pcur[(m) - HIST]))
 #pragma unroll
                 for (int o = 0; o < S; ++o) {
                     {
                         const float4 v = b1[tb * FC + o];
-                        nQM[o] = make_float2(v.x, v.y);
-                        nP[o] = v.z;
+                        Qcur[o] = make_float2(v.x, v.y);
+                        Pcur[o] = v.z;
                     }
-                    float2 a = make_float2(0.f, 0.f);
-                    float bp = 0.f;
+                    float2 a = __fmul2_rn(FSSIM_WQ(o + RAD), KP[RAD]);
+                    float bp = FSSIM_WP(o + RAD) * p.kh[RAD];
 #pragma unroll
-                    for (int tap = 0; tap < TAPS; ++tap) {
-                        const int m = o + tap;
-                        const float2 wq = (m < HIST) ? gQM[m] : nQM[m - HIST];
-                        const float wp = (m < HIST) ? gP[m] : nP[m - HIST];
-                        a = __ffma2_rn(wq, FSSIM_K2(tap), a);
-                        bp = fmaf(wp, FSSIM_K1(tap), bp);
+                    for (int tap = 0; tap < RAD; ++tap) {
+                        a = __ffma2_rn(__fadd2_rn(FSSIM_WQ(o + tap), FSSIM_WQ(o + 2 * RAD - tap)), KP[tap], a);
+                        bp = fmaf(FSSIM_WP(o + tap) + FSSIM_WP(o + 2 * RAD - tap), p.kh[tap], bp);
                     }
                     const int wc = wcg + o;
                     const float2 v = xy[tb * SP + o];
@@ -870,14 +905,24 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
                     if (grow_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc))
                         gg[grow_off + CH32 * static_cast<uint32_t>(wc)] = gv;
                 }
-#pragma unroll
-                for (int m = 0; m < HIST; ++m) {
-                    const int src = m + S;
-                    gQM[m] = (src < HIST) ? gQM[src] : nQM[src - HIST];
-                    gP[m] = (src < HIST) ? gP[src] : nP[src - HIST];
-                }
+#undef FSSIM_WQ
+#undef FSSIM_WP
+                TQ[0] = Qprv[S - 2];
+                TQ[1] = Qprv[S - 1];
+                TP[0] = Pprv[S - 2];
+                TP[1] = Pprv[S - 1];
             }
+#if FSSIM_XY_IN_B
+            cp_async_wait<0>();
+#endif
             __syncthreads();
+        };
+
+        __syncthreads();
+#pragma unroll 1
+        for (int t = 0; t < nslot; t += 2) {
+            bslot(t, A0, A1, B0, B1, Q0, Q1, P0, P1);
+            bslot(t + 1, A1, A0, B1, B0, Q1, Q0, P1, P0);
         }
     }
 #undef FSSIM_K2
