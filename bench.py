@@ -290,7 +290,7 @@ def run_ours(args):
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "peak_kind": f"{peak_kind} (MEASURED_PEAKS.json hbm_gbs)",
                      "traffic": traffic_per_launch(n_local),
-                     "kernel": "fssim::band_kernel<96,true,true>", "kernel_ms": kern * 1e3,
+                     "kernel": "fssim::pipe_kernel<96,true>", "kernel_ms": kern * 1e3,
                      "alg_bytes_per_launch": alg_bytes},
         "cpu_baseline": cpu,
         "e2e": e2e,
