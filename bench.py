@@ -129,7 +129,7 @@ def run_reference(args):
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    sample = 4
+    sample = max(4, -(-2 * threads // C))      # about two (image, channel) planes per host thread
     for _ in range(args.warmup):
         cpu_oracle_rate(sample, threads)
     times = []
@@ -345,6 +345,15 @@ def side_benchmarks(pkg, dev):
     ms = timed(lambda: pkg.dssim_with_gradient_(d, g, x, y, None, True))
     out["batch32_3x256x256_dssim_grad_ms"] = ms
     out["batch32_3x256x256_dssim_grad_hbm_frac"] = x.numel() * 12 / (ms / 1e3) / 1e9 / measured_peaks()[0]
+    # config 4: 64 x 3 x 512 x 512 in N0f8 and in Float16, Float32 gradient, converted in-kernel
+    for tag, dt, nb in (("u8", torch.uint8, 1), ("f16", torch.float16, 2)):
+        x, y = syn.device_pair((3, 512, 512, 64), 0.1, dtype=dt, device=dev)
+        s = torch.empty(64, dtype=torch.float32, device=dev)
+        g = pkg.jl_empty((3, 512, 512, 64), torch.float32, dev)
+        ms = timed(lambda: pkg.ssim_with_gradient_(s, g, x, y, None, True), reps=10)
+        out[f"batch64_3x512x512_{tag}_ssim_grad_ms"] = ms
+        out[f"batch64_3x512x512_{tag}_ssim_grad_hbm_frac"] = x.numel() * (2 * nb + 4) / (ms / 1e3) / 1e9 / measured_peaks()[0]
+        del x, y, g
     return out
 
 
@@ -357,7 +366,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
-    ap.add_argument("--profile-case", choices=["fused", "fwd"], default=None,
+    ap.add_argument("--profile-case", choices=["fused", "fwd", "fused_u8", "fused_f16"], default=None,
                     help="only run the kernel on 64x3x512x512 f32 (a size for ncu captures): "
                          "warmup + steps launches, no timing output")
     args = ap.parse_args()
@@ -377,11 +386,12 @@ def profile_case(args):
     pkg = ge.load_package()
     syn = __import__(pkg.__name__ + ".synthetic", fromlist=["x"])
     shape = (C, H, W, 64)
-    x, y = syn.device_pair(shape, NOISE)
+    dt = {"fused_u8": torch.uint8, "fused_f16": torch.float16}.get(args.profile_case, torch.float32)
+    x, y = syn.device_pair(shape, NOISE, dtype=dt)
     s = torch.empty(64, dtype=torch.float32, device="cuda")
     g = pkg.jl_empty(shape, torch.float32)
     def launch():
-        if args.profile_case == "fused":
+        if args.profile_case.startswith("fused"):
             pkg.ssim_with_gradient_(s, g, x, y, None, True)
         else:
             pkg.ssim_(s, x, y)

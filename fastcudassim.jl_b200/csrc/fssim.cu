@@ -76,40 +76,42 @@ KInfo kinfo()
                  fssim::Geo<NT, S, F, IO>::total, NT, S, NT};
 }
 
-template <int NT, bool WS>
+template <int NT, bool WS, int IOM>
 KInfo pinfo()
 {
-    return KInfo{reinterpret_cast<const void*>(&fssim::pipe_kernel<NT, WS>), fssim::PGeo<NT>::total, NT,
+    return KInfo{reinterpret_cast<const void*>(&fssim::pipe_kernel<NT, WS, IOM>), fssim::PGeo<NT>::total, NT,
                  fssim::PGeo<NT>::S, 2 * NT};
 }
 
-template <int S, bool IO>
-KInfo kernel_info_s(int nt, bool fused, bool want_ssim)
+template <int IOM>
+KInfo pinfo_io(int nt, bool want_ssim)
 {
-    if (fused) {
-        if (want_ssim) {
-            if (nt == 64) return kinfo<64, S, true, true, IO>();
-            return kinfo<96, S, true, true, IO>();
-        }
-        if (nt == 64) return kinfo<64, S, true, false, IO>();
-        return kinfo<96, S, true, false, IO>();
-    }
+    if (nt == 64) return want_ssim ? pinfo<64, true, IOM>() : pinfo<64, false, IOM>();
+    return want_ssim ? pinfo<96, true, IOM>() : pinfo<96, false, IOM>();
+}
+
+template <int S, bool IO>
+KInfo kernel_info_s(int nt, bool /*fused*/, bool /*want_ssim*/)
+{
     if (nt == 64) return kinfo<64, S, false, true, IO>();
     if (nt == 96) return kinfo<96, S, false, true, IO>();
     return kinfo<128, S, false, true, IO>();
 }
 
-// Float32 I/O streams 16 columns per step (cp.async staging); the converting
-// kernels stream 8 (their staging goes through registers).
 #ifndef FSSIM_F32_STEP
 #define FSSIM_F32_STEP 8
 #endif
-// SSIM + gradient with Float32 I/O runs the two-group pipelined kernel.
-KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io)
+// Gradients run the two-group pipelined kernel (32-bit in-image offsets: the
+// caller guarantees C*H*W < 2^31); forward-only SSIM runs the single-group kernel.
+KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io, int iom)
 {
-    if (f32io && fused) {   // (the caller guarantees C*H*W < 2^31: 32-bit in-image offsets)
-        if (nt == 64) return want_ssim ? pinfo<64, true>() : pinfo<64, false>();
-        return want_ssim ? pinfo<96, true>() : pinfo<96, false>();
+    if (fused) {
+        switch (f32io ? 0 : iom) {
+            case 0: return pinfo_io<0>(nt, want_ssim);
+            case fssim::IN_U8: return pinfo_io<fssim::IN_U8>(nt, want_ssim);
+            case fssim::IN_F16: return pinfo_io<fssim::IN_F16>(nt, want_ssim);
+            default: return pinfo_io<fssim::IN_ANY>(nt, want_ssim);
+        }
     }
     return f32io ? kernel_info_s<FSSIM_F32_STEP, true>(nt, fused, want_ssim)
                  : kernel_info_s<8, false>(nt, fused, want_ssim);
@@ -164,7 +166,7 @@ int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 // {64, 96, 128} (forward only) to minimise padded rows, then the number of
 // width segments that best fills the GPU (whole waves of resident CTAs
 // versus the 10-20 warm-up columns each extra segment costs).
-int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f32io, Cfg* cfg)
+int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f32io, int iom, Cfg* cfg)
 {
     Cfg g;
     g.fused = !(flags & FSSIM_SKIP_BACKWARD);
@@ -191,7 +193,7 @@ int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f
             g.nb = static_cast<int>(nb);
         }
     }
-    g.ki = kernel_info(g.nt, g.fused, g.want_ssim, f32io);
+    g.ki = kernel_info(g.nt, g.fused, g.want_ssim, f32io, iom);
     int sms = 0, occ = 0;
     int st = device_facts(g.ki, &sms, &occ);
     if (st != FSSIM_OK) return st;
@@ -261,12 +263,14 @@ int fssim_workspace_size(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t fl
     if (st != FSSIM_OK) return st;
     // The launch geometry (and so the workspace) can differ between the
     // Float32 specialisation and the generic kernels: report the larger need.
-    Cfg g1, g2;
-    st = configure(c, h, w, n, flags, true, &g1);
-    if (st != FSSIM_OK) return st;
-    st = configure(c, h, w, n, flags, false, &g2);
-    if (st != FSSIM_OK) return st;
-    *bytes = std::max(g1.ws_bytes, g2.ws_bytes);
+    size_t most = 0;
+    for (int v = 0; v < 4; ++v) {
+        Cfg g;
+        st = configure(c, h, w, n, flags, v == 0, v == 0 ? fssim::IN_ANY : v, &g);
+        if (st != FSSIM_OK) return st;
+        most = std::max(most, g.ws_bytes);
+    }
+    *bytes = most;
     return ok();
 }
 
@@ -312,10 +316,18 @@ int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimg
     }
     if (!want_ssim && !fused) return ok();   // nothing requested
 
+    if (fused && c * h * w >= (int64_t(1) << 31))
+        return fail(FSSIM_ERR_INVALID_ARGUMENT, "gradient calls need C*H*W < 2^31 elements per image (got %lld)",
+                    (long long)(c * h * w));
     const bool f32io = imgs1_dtype == FSSIM_FLOAT32 && imgs2_dtype == FSSIM_FLOAT32 &&
-                       (!fused || grad_dtype == FSSIM_FLOAT32) && c * h * w < (int64_t(1) << 31);
+                       (!fused || grad_dtype == FSSIM_FLOAT32);
+    const int iom = (imgs1_dtype == FSSIM_N0F8 && imgs2_dtype == FSSIM_N0F8 && grad_dtype == FSSIM_FLOAT32)
+                        ? fssim::IN_U8
+                    : (imgs1_dtype == FSSIM_FLOAT16 && imgs2_dtype == FSSIM_FLOAT16 && grad_dtype == FSSIM_FLOAT32)
+                        ? fssim::IN_F16
+                        : fssim::IN_ANY;
     Cfg g;
-    st = configure(c, h, w, n, flags, f32io, &g);
+    st = configure(c, h, w, n, flags, f32io, fused ? iom : fssim::IN_ANY, &g);
     if (st != FSSIM_OK) return st;
     if (want_ssim) {
         if (!workspace || workspace_bytes < g.ws_bytes)

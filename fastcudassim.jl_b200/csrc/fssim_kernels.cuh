@@ -85,11 +85,45 @@ __device__ __forceinline__ uint32_t ld_raw(const void* base, int dt, int64_t idx
     return __ldg(reinterpret_cast<const unsigned char*>(base) + idx);
 }
 
-__device__ __forceinline__ float cvt_raw(uint32_t r, int dt, const float* lut)
+// N0f8 -> Float32: the correctly rounded value of raw/255.  q = raw * fl(1/255)
+// is off by one ulp for about half of the 256 bytes; one Newton correction step
+// for a constant divisor (residual e = raw - 255 q by FMA, then q + e * fl(1/255))
+// gives the correctly rounded quotient for every byte (checked exhaustively, and
+// against the division by a GPU test).
+__device__ __forceinline__ float n0f8_to_f32(uint32_t r)
+{
+    const float inv = 1.0f / 255.0f;
+    const float fr = static_cast<float>(r & 255u);
+    const float q = fr * inv;
+    const float e = fmaf(-q, 255.0f, fr);
+    return fmaf(e, inv, q);
+}
+
+__device__ __forceinline__ float cvt_raw(uint32_t r, int dt, const float* /*unused*/)
 {
     if (dt == DT_F32) return __uint_as_float(r);
     if (dt == DT_F16) return __half2float(__ushort_as_half(static_cast<unsigned short>(r)));
-    return lut[r & 255u];
+    return n0f8_to_f32(r);
+}
+
+// Input modes of the converting kernels: both inputs N0f8, both Float16, or any
+// mix (dtype read at run time).
+enum InMode { IN_U8 = 1, IN_F16 = 2, IN_ANY = 3 };
+
+template <int IM>
+__device__ __forceinline__ uint32_t ld_in(const void* base, int dt, int64_t idx)
+{
+    if (IM == IN_U8) return __ldg(reinterpret_cast<const unsigned char*>(base) + idx);
+    if (IM == IN_F16) return __ldg(reinterpret_cast<const unsigned short*>(base) + idx);
+    return ld_raw(base, dt, idx);
+}
+
+template <int IM>
+__device__ __forceinline__ float cvt_in(uint32_t r, int dt)
+{
+    if (IM == IN_U8) return n0f8_to_f32(r);
+    if (IM == IN_F16) return __half2float(__ushort_as_half(static_cast<unsigned short>(r)));
+    return cvt_raw(r, dt, nullptr);
 }
 
 __device__ __forceinline__ void st_grad(void* base, int dt, int64_t idx, float v)
@@ -149,9 +183,8 @@ struct Geo {
     static constexpr int f1_bytes = R1 * FC * 16;
     static constexpr int qmp_bytes = FUSED ? QROWS * FC * 16 : 0;
     static constexpr int b1_bytes = FUSED ? NT * FC * 16 : 0;
-    static constexpr int lut_bytes = F32IO ? 0 : 256 * 4;
     static constexpr int red_bytes = (NT / 32 + 2) * 8;
-    static constexpr int total = stage_bytes + f1_bytes + qmp_bytes + b1_bytes + lut_bytes + red_bytes;
+    static constexpr int total = stage_bytes + f1_bytes + qmp_bytes + b1_bytes + red_bytes;
     static_assert(R1 % V == 0 && NT % 32 == 0, "band geometry");
     static_assert((S * NRUN1) % NT == 0, "F1 items must divide evenly over the CTA");
     static_assert(NRUNB * V <= NT, "B1 rows must fit the B2 buffer");
@@ -207,7 +240,7 @@ __device__ __forceinline__ void finish_image(const Params& p, int n, int local_c
 // memory with cp.async (double-buffered, two steps ahead) and no conversion;
 // otherwise elements are loaded by type, converted, and staged through registers.
 template <int NT, int S, bool FUSED, bool WANT_SSIM, bool F32IO>
-__global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
+__global__ void __launch_bounds__(NT, (FUSED || !F32IO) ? 2 : 3) band_kernel(const Params p)
 {
     using G = Geo<NT, S, FUSED, F32IO>;
     constexpr int R1 = G::R1, T = G::T, R2 = G::R2, LAG = G::LAG;
@@ -219,7 +252,6 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
     float4* f1buf = reinterpret_cast<float4*>(smem_raw + G::stage_bytes);
     float4* qmp = reinterpret_cast<float4*>(smem_raw + G::stage_bytes + G::f1_bytes);
     float4* b1buf = reinterpret_cast<float4*>(smem_raw + G::stage_bytes + G::f1_bytes + G::qmp_bytes);
-    float* lut = reinterpret_cast<float*>(smem_raw + G::stage_bytes + G::f1_bytes + G::qmp_bytes + G::b1_bytes);
     double* red = reinterpret_cast<double*>(smem_raw + G::total - G::red_bytes);
 
     const int tid = threadIdx.x;
@@ -248,8 +280,6 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
 #define FSSIM_K2(tap) KP[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
 #define FSSIM_K1(tap) p.kh[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
 
-    if (!F32IO)
-        for (int i = tid; i < 256; i += NT) lut[i] = __fdiv_rn(static_cast<float>(i), 255.0f);
     if (FUSED)
         for (int e = tid; e < (QROWS - R1) * FC; e += NT) qmp[R1 * FC + e] = make_float4(0.f, 0.f, 0.f, 0.f);
 
@@ -310,7 +340,7 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
             const int e = tid + NT * u;
             if (e < R2 * S) {
                 const int i = e % R2, j = e / R2;
-                stage[i * SP + j] = make_float2(cvt_raw(rx[u], p.xdt, lut), cvt_raw(ry[u], p.ydt, lut));
+                stage[i * SP + j] = make_float2(cvt_raw(rx[u], p.xdt, nullptr), cvt_raw(ry[u], p.ydt, nullptr));
             }
         }
     };
@@ -321,7 +351,6 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
         cp_async_wait<1>();
     } else {
         issue_loads(0);
-        __syncthreads();   // lut ready
         store_stage();
         issue_loads(1);
     }
@@ -515,8 +544,8 @@ __global__ void __launch_bounds__(NT, FUSED ? 2 : 3) band_kernel(const Params p)
                         xv = __ldg(reinterpret_cast<const float*>(p.x) + g);
                         yv = __ldg(reinterpret_cast<const float*>(p.y) + g);
                     } else {
-                        xv = cvt_raw(ld_raw(p.x, p.xdt, g), p.xdt, lut);
-                        yv = cvt_raw(ld_raw(p.y, p.ydt, g), p.ydt, lut);
+                        xv = cvt_raw(ld_raw(p.x, p.xdt, g), p.xdt, nullptr);
+                        yv = cvt_raw(ld_raw(p.y, p.ydt, g), p.ydt, nullptr);
                     }
                     // src/core.jl:773-782: (2 x K(dQ) + K(dM) + y K(dP)) * N_inv (N_inv folded upstream)
                     const float gv = fmaf(yv, bp, fmaf(xv, a.x, a.y));
@@ -602,9 +631,15 @@ struct PGeo {
     static_assert(stage_one % 16 == 0 && xy_one % 16 == 0, "16-byte alignment of the buffers");
 };
 
-template <int NT, bool WANT_SSIM>
+// IOM 0: Float32 inputs and gradient; inputs go to shared memory with cp.async.
+// Otherwise (IOM = InMode) group A loads raw elements into registers one slot
+// ahead, converts them (Float16 exactly, N0f8 as the correctly rounded raw/255)
+// and stores them at the end of the slot; with IN_ANY the gradient is stored in
+// its own dtype, the other modes write Float32.
+template <int NT, bool WANT_SSIM, int IOM>
 __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Params p)
 {
+    constexpr bool F32IO = IOM == 0;   // Float32 inputs and gradient (cp.async staging)
     using G = PGeo<NT>;
     constexpr int S = G::S, R1 = G::R1, T = G::T, R2 = G::R2, LAG = G::LAG;
     constexpr int SP = G::SP, FC = G::FC, NRUNB = G::NRUNB, QROWS = G::QROWS;
@@ -634,9 +669,10 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
     const int Lc = wend - w0;
     // In-image element offsets are 32-bit (the host guarantees C*H*W < 2^31), so
     // each address is one wide multiply-add from the image base.
-    const float* __restrict__ xg = reinterpret_cast<const float*>(p.x) + static_cast<int64_t>(n) * p.img_elems + c;
-    const float* __restrict__ yg = reinterpret_cast<const float*>(p.y) + static_cast<int64_t>(n) * p.img_elems + c;
-    float* __restrict__ gg = reinterpret_cast<float*>(p.grad) + static_cast<int64_t>(n) * p.img_elems + c;
+    const int64_t ibase = static_cast<int64_t>(n) * p.img_elems + c;   // element index of (c, 0, 0, n)
+    const float* __restrict__ xg = reinterpret_cast<const float*>(p.x) + ibase;   // (F32IO)
+    const float* __restrict__ yg = reinterpret_cast<const float*>(p.y) + ibase;
+    float* __restrict__ gg = reinterpret_cast<float*>(p.grad) + ibase;
     const uint32_t CH32 = static_cast<uint32_t>(C) * static_cast<uint32_t>(H);
     const int ns = (Lc + 2 * LAG - 1) / S + 1;
     const int nslot = (ns + G::LATENCY + 1) & ~1;   // even: group B runs two slots per iteration
@@ -704,17 +740,77 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
             }
         };
 
-        issue_stage(0, stage);
-        cp_async_commit();
-        cp_async_wait<0>();
+        // converting loaders: raw bits of step k (or of B2's pixels of step k) in
+        // registers, converted and stored into shared memory by the store_* calls
+        uint32_t rsx[F32IO ? 1 : G::LROWS * S], rsy[F32IO ? 1 : G::LROWS * S];
+        uint32_t rxx[F32IO ? 1 : S], rxy[F32IO ? 1 : S];
+        auto load_stage_raw = [&](int k) {
+            const int cb = w0 - LAG + k * S;
+#pragma unroll
+            for (int j = 0; j < (F32IO ? 0 : S); ++j) {
+                const int wc = cb + j;
+                const bool colok = static_cast<unsigned>(wc) < static_cast<unsigned>(W);
+#pragma unroll
+                for (int r = 0; r < G::LROWS; ++r) {
+                    const bool ok = lrow_ok[r] && colok;
+                    const int64_t g = ibase + (lrow_off[r] + CH32 * static_cast<uint32_t>(colok ? wc : 0));
+                    rsx[r * S + j] = ok ? ld_in<IOM>(p.x, p.xdt, g) : 0u;
+                    rsy[r * S + j] = ok ? ld_in<IOM>(p.y, p.ydt, g) : 0u;
+                }
+            }
+        };
+        auto store_stage_raw = [&](float2* buf) {
+#pragma unroll
+            for (int j = 0; j < (F32IO ? 0 : S); ++j) {
+#pragma unroll
+                for (int r = 0; r < G::LROWS; ++r) {
+                    const int i = ta + NT * r;
+                    if (G::LROWS == 1 || i < R2)
+                        buf[i * SP + j] = make_float2(cvt_in<IOM>(rsx[r * S + j], p.xdt),
+                                                      cvt_in<IOM>(rsy[r * S + j], p.ydt));
+                }
+            }
+        };
+        auto load_xy_raw = [&](int k) {
+            const int cb = w0 - LAG + k * S - 2 * RAD;
+#pragma unroll
+            for (int o = 0; o < (F32IO ? 0 : S); ++o) {
+                const int wc = cb + o;
+                const bool ok = xyrow_ok && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc);
+                const int64_t g = ibase + (xyrow_off + CH32 * static_cast<uint32_t>(ok ? wc : 0));
+                rxx[o] = ok ? ld_in<IOM>(p.x, p.xdt, g) : 0u;
+                rxy[o] = ok ? ld_in<IOM>(p.y, p.ydt, g) : 0u;
+            }
+        };
+        auto store_xy_raw = [&](float2* buf) {
+#pragma unroll
+            for (int o = 0; o < (F32IO ? 0 : S); ++o)
+                buf[ta * SP + o] = make_float2(cvt_in<IOM>(rxx[o], p.xdt), cvt_in<IOM>(rxy[o], p.ydt));
+        };
+
+        if (F32IO) {
+            issue_stage(0, stage);
+            cp_async_commit();
+            cp_async_wait<0>();
+        } else {
+            load_stage_raw(0);
+            store_stage_raw(stage);
+        }
         __syncthreads();
 #pragma unroll 1
         for (int t = 0; t < nslot; ++t) {
-            if (t + 1 < ns) issue_stage(t + 1, stage + ((t + 1) & 1) * STG);
+            const bool next_stage = t + 1 < ns;
+            const bool next_xy = t >= 2 && t - 2 < ns;
+            if (F32IO) {
+                if (next_stage) issue_stage(t + 1, stage + ((t + 1) & 1) * STG);
 #if !FSSIM_XY_IN_B
-            if (t >= 2 && t - 2 < ns) issue_xy(t - 2, xyb + ((t + 1) & 1) * XYN);
+                if (next_xy) issue_xy(t - 2, xyb + ((t + 1) & 1) * XYN);
 #endif
-            cp_async_commit();
+                cp_async_commit();
+            } else {
+                if (next_stage) load_stage_raw(t + 1);
+                if (next_xy) load_xy_raw(t - 2);
+            }
             // -------- F1(t): h-direction pass of the 4 moment images --------
             if (t < ns) {
                 const float2* st = stage + (t & 1) * STG;
@@ -771,7 +867,12 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
                 for (int o = 0; o < V; ++o)
                     b1[(V * q1 + o) * FC + j1] = make_float4(aQM[o].x, aQM[o].y, aP[o], 0.f);
             }
-            cp_async_wait<0>();
+            if (F32IO) {
+                cp_async_wait<0>();
+            } else {
+                if (next_stage) store_stage_raw(stage + ((t + 1) & 1) * STG);
+                if (next_xy) store_xy_raw(xyb + ((t + 1) & 1) * XYN);
+            }
             __syncthreads();
         }
     } else {
@@ -902,8 +1003,11 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
                     const float2 v = xy[tb * SP + o];
                     // src/core.jl:773-782: (2 x K(dQ) + K(dM) + y K(dP)) * N_inv (N_inv folded upstream)
                     const float gv = fmaf(v.y, bp, fmaf(v.x, a.x, a.y));
-                    if (grow_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc))
-                        gg[grow_off + CH32 * static_cast<uint32_t>(wc)] = gv;
+                    if (grow_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc)) {
+                        const uint32_t off = grow_off + CH32 * static_cast<uint32_t>(wc);
+                        if (IOM != IN_ANY) gg[off] = gv;
+                        else st_grad(p.grad, p.gdt, ibase + off, gv);
+                    }
                 }
 #undef FSSIM_WQ
 #undef FSSIM_WP

@@ -80,3 +80,22 @@ def test_synthetic_generator_is_reproducible(pkg):
     assert a.flags.f_contiguous and a.dtype == np.float32 and 0 <= a.min() and a.max() < 1
     x, y = syn.host_pair(5, (2, 50, 40, 1), 0.1)
     assert 0 <= y.min() and y.max() <= 1 and abs(float(np.std(y - x)) - 0.1) < 0.02
+
+
+def test_n0f8_conversion_formula_is_correctly_rounded():
+    """The kernels convert N0f8 with q = r*fl(1/255) and one FMA correction
+    (q + fma(-q, 255, r) * fl(1/255)); exact rational arithmetic shows it equals
+    the correctly rounded r/255 for all 256 bytes (FixedPointNumbers' value)."""
+    from fractions import Fraction
+
+    def rne32(q: Fraction) -> np.float32:
+        c = np.float32(float(q))
+        cands = [np.nextafter(c, np.float32(-1)), c, np.nextafter(c, np.float32(2))]
+        return min(cands, key=lambda v: (abs(Fraction(float(v)) - q), int(np.array(v).view(np.uint32)) & 1))
+
+    inv = np.float32(1.0) / np.float32(255.0)
+    for r in range(256):
+        q = np.float32(np.float32(r) * inv)
+        e = rne32(Fraction(float(-q)) * 255 + r)
+        got = rne32(Fraction(float(e)) * Fraction(float(inv)) + Fraction(float(q)))
+        assert got == rne32(Fraction(r, 255)), r
