@@ -101,6 +101,13 @@ KInfo kernel_info_s(int nt, bool /*fused*/, bool /*want_ssim*/)
 #ifndef FSSIM_F32_STEP
 #define FSSIM_F32_STEP 8
 #endif
+template <bool F, bool WS>
+KInfo finfo()
+{
+    return KInfo{reinterpret_cast<const void*>(&fssim::f64_kernel<F, WS>), fssim::D64Geo::total, fssim::D64Geo::TO,
+                 fssim::D64Geo::TO, fssim::D64Geo::NT};
+}
+
 // Gradients run the two-group pipelined kernel (32-bit in-image offsets: the
 // caller guarantees C*H*W < 2^31); forward-only SSIM runs the single-group kernel.
 KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io, int iom)
@@ -162,6 +169,8 @@ struct Cfg {
 
 int64_t cdiv(int64_t a, int64_t b) { return (a + b - 1) / b; }
 
+constexpr int IOM_F64 = 4;   // configure(): compute in double precision
+
 // Launch geometry: band height from {54, 86, 118} rows (gradient kernels) or
 // {64, 96, 128} (forward only) to minimise padded rows, then the number of
 // width segments that best fills the GPU (whole waves of resident CTAs
@@ -172,6 +181,23 @@ int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f
     g.fused = !(flags & FSSIM_SKIP_BACKWARD);
     g.want_ssim = !(flags & FSSIM_SKIP_SSIM);
     if (!g.fused && !g.want_ssim) {
+        *cfg = g;
+        return FSSIM_OK;
+    }
+    if (iom == IOM_F64) {   // double precision: one 16 x 16 tile per CTA
+        g.ki = g.fused ? (g.want_ssim ? finfo<true, true>() : finfo<true, false>()) : finfo<false, true>();
+        int sms = 0, occ = 0;
+        int st = device_facts(g.ki, &sms, &occ);
+        if (st != FSSIM_OK) return st;
+        g.nt = fssim::D64Geo::TO;
+        g.T = fssim::D64Geo::TO;
+        g.nb = static_cast<int>(cdiv(h, fssim::D64Geo::TO));
+        g.nseg = static_cast<int>(cdiv(w, fssim::D64Geo::TO));
+        g.L = fssim::D64Geo::TO;
+        g.cpi = c * g.nb * g.nseg;
+        g.grid = n * g.cpi;
+        g.ws_counters = ((static_cast<size_t>(n) * sizeof(unsigned) + 255) / 256) * 256;
+        g.ws_bytes = g.want_ssim ? g.ws_counters + static_cast<size_t>(n) * g.cpi * sizeof(double) : 0;
         *cfg = g;
         return FSSIM_OK;
     }
@@ -224,7 +250,10 @@ int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f
     return FSSIM_OK;
 }
 
-bool is_input_dtype(int d) { return d == FSSIM_FLOAT32 || d == FSSIM_FLOAT16 || d == FSSIM_N0F8; }
+bool is_input_dtype(int d)
+{
+    return d == FSSIM_FLOAT32 || d == FSSIM_FLOAT16 || d == FSSIM_N0F8 || d == FSSIM_FLOAT64;
+}
 bool is_float_dtype(int d) { return d == FSSIM_FLOAT32 || d == FSSIM_FLOAT16 || d == FSSIM_FLOAT64; }
 size_t dsize(int d) { return d == FSSIM_FLOAT32 ? 4 : d == FSSIM_FLOAT16 ? 2 : d == FSSIM_N0F8 ? 1 : 8; }
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
@@ -264,7 +293,7 @@ int fssim_workspace_size(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t fl
     // The launch geometry (and so the workspace) can differ between the
     // Float32 specialisation and the generic kernels: report the larger need.
     size_t most = 0;
-    for (int v = 0; v < 4; ++v) {
+    for (int v = 0; v <= IOM_F64; ++v) {
         Cfg g;
         st = configure(c, h, w, n, flags, v == 0, v == 0 ? fssim::IN_ANY : v, &g);
         if (st != FSSIM_OK) return st;
@@ -287,7 +316,7 @@ int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimg
     if (st != FSSIM_OK) return st;
     if (!imgs1 || !imgs2) return fail(FSSIM_ERR_INVALID_ARGUMENT, "imgs1 and imgs2 must not be NULL");
     if (!is_input_dtype(imgs1_dtype) || !is_input_dtype(imgs2_dtype))
-        return fail(FSSIM_ERR_UNSUPPORTED_DTYPE, "image dtypes must be FLOAT32, FLOAT16 or N0F8 (got %d, %d)",
+        return fail(FSSIM_ERR_UNSUPPORTED_DTYPE, "image dtypes must be FLOAT32, FLOAT16, N0F8 or FLOAT64 (got %d, %d)",
                     imgs1_dtype, imgs2_dtype);
     if (!aligned(imgs1, dsize(imgs1_dtype)) || !aligned(imgs2, dsize(imgs2_dtype)))
         return fail(FSSIM_ERR_MISALIGNED, "image pointers must be aligned to their element size");
@@ -326,8 +355,10 @@ int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimg
                     : (imgs1_dtype == FSSIM_FLOAT16 && imgs2_dtype == FSSIM_FLOAT16 && grad_dtype == FSSIM_FLOAT32)
                         ? fssim::IN_F16
                         : fssim::IN_ANY;
+    // Float64 on either input: compute in double (promote_type(T1, T2, Float32), src/core.jl:953-954)
+    const bool f64 = imgs1_dtype == FSSIM_FLOAT64 || imgs2_dtype == FSSIM_FLOAT64;
     Cfg g;
-    st = configure(c, h, w, n, flags, f32io, fused ? iom : fssim::IN_ANY, &g);
+    st = configure(c, h, w, n, flags, f32io && !f64, f64 ? IOM_F64 : (fused ? iom : fssim::IN_ANY), &g);
     if (st != FSSIM_OK) return st;
     if (want_ssim) {
         if (!workspace || workspace_bytes < g.ws_bytes)

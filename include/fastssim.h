@@ -92,9 +92,11 @@ int fssim_workspace_size(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t fl
  *               previous contents are added to the map sums before the division,
  *               as the reference's accumulation into N_ssims does (src/core.jl:919-922).
  *  ssims_len    must equal n (src/core.jl:967-969).
- *  dL_dimgs1    gradient, canonical (C,H,W,N) (dtype FLOAT32 or FLOAT16).  Required
+ *  dL_dimgs1    gradient, canonical (C,H,W,N) (dtype FLOAT32, FLOAT16 or FLOAT64).  Required
  *               unless FSSIM_SKIP_BACKWARD.
- *  imgs1, imgs2 canonical (C,H,W,N) inputs (dtype FLOAT32, FLOAT16 or N0F8 each).
+ *  imgs1, imgs2 canonical (C,H,W,N) inputs (dtype FLOAT32, FLOAT16, N0F8 or FLOAT64 each).
+ *               With a FLOAT64 input the whole computation runs in double precision,
+ *               as the reference's promote_type(T1, T2, Float32) does (src/core.jl:953-954).
  *  qmp          the reference's N_dssims_dQMP buffer (h,3,c,w,n).  Accepted for
  *               interface parity and never read or written: the fused kernel keeps
  *               the partial gradients on chip.  May be NULL.

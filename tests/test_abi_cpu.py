@@ -38,7 +38,7 @@ def test_version_and_error_channel(pkg):
     st = lib.fssim_fwd_bwd(None, 0, 1, None, 0, ctypes.c_void_p(16), 0, ctypes.c_void_p(16), 0, None,
                            0, 1, 1, 1, 0, None, 0, None)
     assert st == pkg._native.ERR_INVALID_ARGUMENT
-    st = lib.fssim_fwd_bwd(None, 0, 1, None, 0, ctypes.c_void_p(16), 3, ctypes.c_void_p(16), 0, None,
+    st = lib.fssim_fwd_bwd(None, 0, 1, None, 0, ctypes.c_void_p(16), 7, ctypes.c_void_p(16), 0, None,
                            1, 1, 1, 1, 0, None, 0, None)
     assert st == pkg._native.ERR_UNSUPPORTED_DTYPE
     st = lib.fssim_fwd_bwd(ctypes.c_void_p(16), 0, 2, None, 0, ctypes.c_void_p(16), 0, ctypes.c_void_p(16), 0,

@@ -177,3 +177,37 @@ def test_golden_scipy_cases(pkg, golden):
         # smooth ramps: the Float32 algorithm itself sits ~8e-5 from float64 there
         tol = 2e-4 if name.startswith("ramps") else GRAD_RTOL_L2
         assert _rel_l2(g, c["grad"]) <= tol, (name, _rel_l2(g, c["grad"]))
+
+
+@pytest.mark.parametrize("xdt,ydt", [(np.float64, np.float64), (np.float32, np.float64), (np.float64, np.uint8)])
+@pytest.mark.parametrize("shape", [(3, 53, 41, 2), (1, 37, 5, 1), (2, 128, 96, 1)])
+def test_float64_inputs_compute_in_double(pkg, orc, xdt, ydt, shape):
+    """Float64 on either input: the whole computation runs in double precision, and
+    the allocated outputs are Float64 (promote_type(T1, T2, Float32), src/core.jl:953-954;
+    test/eltypes.jl:13,24-25)."""
+    syn = _syn(pkg)
+    x, y = syn.host_pair(61, shape, 0.1, dtype=np.float64)
+    x8, y8 = syn.host_pair(61, shape, 0.1, dtype=np.uint8)
+    x = x8 if xdt == np.uint8 else np.asfortranarray(x.astype(xdt))
+    y = y8 if ydt == np.uint8 else np.asfortranarray(y.astype(ydt))
+    xt, yt = pkg.jl_from_numpy(x), pkg.jl_from_numpy(y)
+    for dssim, div2 in ((False, False), (True, True)):
+        if dssim:
+            v, g = pkg.dssim_with_gradient(xt, yt, div2)
+        else:
+            v, g = pkg.ssim_with_gradient(xt, yt)
+        assert v.dtype == torch.float64 and g.dtype == torch.float64
+        rv, rg = orc.ssim(x, y, flags=_flags(orc, dssim, div2), precision="f64")
+        assert np.max(np.abs(v.cpu().numpy() - rv)) <= 1e-10
+        assert _rel_l2(pkg.jl_to_numpy(g), rg) <= 1e-9
+        fv = pkg.dssim(xt, yt, div2) if dssim else pkg.ssim(xt, yt)
+        assert np.max(np.abs(fv.cpu().numpy() - rv)) <= 1e-10
+
+
+def test_float64_gradient_output_from_float32_inputs(pkg, orc):
+    x, y = _syn(pkg).host_pair(62, (3, 64, 48, 2), 0.1)
+    xt, yt = pkg.jl_from_numpy(x), pkg.jl_from_numpy(y)
+    g = pkg.jl_empty((3, 64, 48, 2), torch.float64)
+    pkg.ssim_gradient_(g, xt, yt, None)
+    _, rg = orc.ssim(x, y, precision="f32")
+    assert _rel_l2(pkg.jl_to_numpy(g), rg) <= GRAD_RTOL_L2

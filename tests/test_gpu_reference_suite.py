@@ -148,6 +148,18 @@ def test_eltype_promotion_synthetic(pkg):
     x16 = pkg.jl_from_numpy(np.asfortranarray(x32.astype(np.float16)))
     y16 = pkg.jl_from_numpy(np.asfortranarray(y32.astype(np.float16)))
     assert isinstance(pkg.ssim(x16, y16), float)
+    # Float32 with Float64 -> Float64 (test/eltypes.jl:13); N0f8 == Float32 == Float64 values (:16-18)
+    x64 = pkg.jl_from_numpy(np.asfortranarray(x32.astype(np.float64)))
+    y64 = pkg.jl_from_numpy(np.asfortranarray(y32.astype(np.float64)))
+    s64 = pkg.ssim(x64, y64)
+    assert isinstance(s64, float) and s64 == pytest.approx(s32, rel=RTOL) and s64 == pytest.approx(s8, rel=RTOL)
+    xb = pkg.jl_reshape(pkg.jl_from_numpy(np.asfortranarray(x32)), (3, 96, 96, 1))
+    yb = pkg.jl_reshape(y64, (3, 96, 96, 1))
+    sb = pkg.ssim(xb, yb)
+    assert sb.dtype == torch.float64
+    # the gradient follows the first image's format, promoted (test/eltypes.jl:24-25)
+    assert pkg.ssim_gradient(x64, pkg.jl_from_numpy(np.asfortranarray(x8))).dtype == torch.float64
+    assert pkg.ssim_gradient(pkg.jl_from_numpy(np.asfortranarray(x8)), x64).dtype == torch.float64
 
 
 def test_autodiff(pkg):
