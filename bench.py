@@ -354,6 +354,18 @@ def side_benchmarks(pkg, dev):
         out[f"batch64_3x512x512_{tag}_ssim_grad_ms"] = ms
         out[f"batch64_3x512x512_{tag}_ssim_grad_hbm_frac"] = x.numel() * (2 * nb + 4) / (ms / 1e3) / 1e9 / measured_peaks()[0]
         del x, y, g
+    # one autograd step (values, then the pullback of a per-image cotangent) on 64 x 3 x 512 x 512:
+    # the reference's rrule (gradient with the values, broadcast in the pullback) against the
+    # deferred rule (values only, then one gradient launch with the cotangent folded in)
+    x, y = syn.device_pair((3, 512, 512, 64), 0.1, device=dev)
+    x.requires_grad_(True)
+    cot = torch.linspace(-1.0, 1.0, 64, device=dev)
+    for tag, defer in (("eager", False), ("deferred", True)):
+        def step():
+            x.grad = None
+            pkg.dssim_autograd(x, y, defer_gradient=defer).backward(cot)
+        out[f"autograd_dssim_64x3x512x512_{tag}_ms"] = timed(step, reps=10)
+    del x, y
     return out
 
 

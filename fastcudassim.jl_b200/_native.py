@@ -30,7 +30,7 @@ ERR_MISALIGNED = 5
 ERR_CUDA = 6
 
 EXPORTED_SYMBOLS = ("fssim_version", "fssim_last_error", "fssim_workspace_size", "fssim_fwd_bwd",
-                    "fssim_fwd_bwd_noalloc")
+                    "fssim_fwd_bwd_scaled", "fssim_fwd_bwd_noalloc")
 # Size of the scratch array behind fssim_fwd_bwd_noalloc (FSSIM_NOALLOC_SCRATCH_BYTES).
 NOALLOC_SCRATCH_BYTES = 4 << 20
 
@@ -69,6 +69,9 @@ def load() -> ctypes.CDLL:
     lib.fssim_fwd_bwd.argtypes = [vp, ctypes.c_int, i64, vp, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int,
                                   vp, i64, i64, i64, i64, u32, vp, sz, vp]
     lib.fssim_fwd_bwd.restype = ctypes.c_int
+    lib.fssim_fwd_bwd_scaled.argtypes = [vp, ctypes.c_int, i64, vp, ctypes.c_int, vp, ctypes.c_int, vp,
+                                         ctypes.c_int, i64, i64, i64, i64, u32, vp, ctypes.c_int, vp, sz, vp]
+    lib.fssim_fwd_bwd_scaled.restype = ctypes.c_int
     lib.fssim_fwd_bwd_noalloc.argtypes = [vp, ctypes.c_int, i64, vp, ctypes.c_int, vp, ctypes.c_int, vp,
                                           ctypes.c_int, i64, i64, i64, i64, u32, vp]
     lib.fssim_fwd_bwd_noalloc.restype = ctypes.c_int
@@ -108,6 +111,16 @@ def fwd_bwd(ssims_ptr: int, ssims_dtype: int, ssims_len: int, grad_ptr: int, gra
     check(load().fssim_fwd_bwd(ssims_ptr or None, ssims_dtype, ssims_len, grad_ptr or None, grad_dtype,
                                x_ptr or None, x_dtype, y_ptr or None, y_dtype, qmp_ptr or None,
                                c, h, w, n, flags, ws_ptr or None, ws_bytes, stream or None))
+
+
+def fwd_bwd_scaled(ssims_ptr: int, ssims_dtype: int, ssims_len: int, grad_ptr: int, grad_dtype: int,
+                   x_ptr: int, x_dtype: int, y_ptr: int, y_dtype: int, c: int, h: int, w: int, n: int,
+                   flags: int, scale_ptr: int, scale_dtype: int, ws_ptr: int, ws_bytes: int, stream: int) -> None:
+    """``fssim_fwd_bwd_scaled``: the gradient of image i comes out multiplied by
+    ``scale[i]`` (the pullback's cotangent), with no separate broadcast."""
+    check(load().fssim_fwd_bwd_scaled(ssims_ptr or None, ssims_dtype, ssims_len, grad_ptr or None, grad_dtype,
+                                      x_ptr or None, x_dtype, y_ptr or None, y_dtype, c, h, w, n, flags,
+                                      scale_ptr or None, scale_dtype, ws_ptr or None, ws_bytes, stream or None))
 
 
 def fwd_bwd_noalloc(ssims_ptr: int, ssims_dtype: int, ssims_len: int, grad_ptr: int, grad_dtype: int,

@@ -6,12 +6,20 @@ and differentiate with respect to ``imgs1``; ``imgs2`` and the flag get no
 gradient.  As in the reference rrule (ext/...:19-44, :54-73) the forward pass
 computes values and gradient in one call, and the pullback scales the stored
 gradient IN PLACE by the cotangent, broadcast over the batch axis.
+
+``defer_gradient=True`` is an alternative with no counterpart in the
+reference: the forward pass computes only the values (the forward-only
+kernel) and keeps the inputs; the pullback computes the gradient with the
+cotangent folded into the kernel as a per-image factor
+(``fssim_fwd_bwd_scaled``).  No gradient array lives between the two passes
+and no broadcast pass runs, at the price of reading the inputs twice.
 """
 from __future__ import annotations
 
 import torch
 
-from .interface import dssim_with_gradient, ssim_with_gradient
+from .core import ssim_fwd_bwd
+from .interface import dssim, dssim_with_gradient, ssim, ssim_with_gradient
 
 
 class _SSIMRule(torch.autograd.Function):
@@ -40,11 +48,35 @@ class _SSIMRule(torch.autograd.Function):
         return g, None, None, None
 
 
-def ssim_autograd(imgs1, imgs2):
+class _DeferredSSIMRule(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, imgs1, imgs2, use_dssim: bool, divide_by_two: bool):
+        x, y = imgs1.detach(), imgs2.detach()
+        vals = dssim(x, y, divide_by_two) if use_dssim else ssim(x, y)
+        if not isinstance(vals, torch.Tensor):
+            vals = torch.tensor(vals, dtype=torch.float64 if torch.float64 in (x.dtype, y.dtype) else torch.float32,
+                                device=x.device)
+        ctx.inputs = (x, y)
+        ctx.use_dssim = use_dssim
+        ctx.divide_by_two = divide_by_two
+        return vals
+
+    @staticmethod
+    def backward(ctx, cot):
+        x, y = ctx.inputs
+        ctx.inputs = None
+        _, g = ssim_fwd_bwd(None, None, x, y, None, False, True, False, ctx.use_dssim, ctx.divide_by_two,
+                            grad_scale=cot.detach().reshape(-1))
+        return g, None, None, None
+
+
+def ssim_autograd(imgs1, imgs2, defer_gradient: bool = False):
     """Differentiable ``ssim`` (ext/FastCUDASSIMChainRulesCoreExt.jl:15-45)."""
-    return _SSIMRule.apply(imgs1, imgs2, False, False)
+    rule = _DeferredSSIMRule if defer_gradient else _SSIMRule
+    return rule.apply(imgs1, imgs2, False, False)
 
 
-def dssim_autograd(imgs1, imgs2, divide_by_two_in_dssim=False):
+def dssim_autograd(imgs1, imgs2, divide_by_two_in_dssim=False, defer_gradient: bool = False):
     """Differentiable ``dssim`` (ext/FastCUDASSIMChainRulesCoreExt.jl:54-74)."""
-    return _SSIMRule.apply(imgs1, imgs2, True, bool(divide_by_two_in_dssim))
+    rule = _DeferredSSIMRule if defer_gradient else _SSIMRule
+    return rule.apply(imgs1, imgs2, True, bool(divide_by_two_in_dssim))

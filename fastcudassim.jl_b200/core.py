@@ -61,13 +61,20 @@ def _require_device_array(name: str, t: torch.Tensor) -> None:
 
 
 def ssim_fwd_bwd(ssims, dL_dimgs1, imgs1, imgs2, N_dssims_dQMP, should_zero: bool,
-                 skip_ssim: bool, skip_backward: bool, use_dssim: bool, divide_by_two_in_dssim: bool):
+                 skip_ssim: bool, skip_backward: bool, use_dssim: bool, divide_by_two_in_dssim: bool,
+                 grad_scale: torch.Tensor | None = None):
     """``_ssim_fwd_bwd!`` (src/core.jl:933-1107).  Returns ``(ssims, dL_dimgs1)``.
 
     Arguments that are ``None`` are allocated (outputs) or not needed (the
     intermediate buffer: the fused kernel keeps the partial gradients on chip).
     An allocated ``ssims`` for an input without a batch axis comes back as a
-    Python float (src/conversions.jl:98-106)."""
+    Python float (src/conversions.jl:98-106).
+
+    ``grad_scale`` (no counterpart in the reference driver) is an optional
+    device vector with one factor per image: the gradient of image i comes out
+    multiplied by it, which is the rrule's ``dL_dimgs1 .*= reshape(dL_dssims, 1,
+    1, 1, :)`` (ext/FastCUDASSIMChainRulesCoreExt.jl:28-36) done inside the
+    kernel (``fssim_fwd_bwd_scaled``)."""
     # Shape rules first, as in the reference (src/core.jl:942-984); the device
     # check comes after them, where the reference would fail on a CPU array.
     cimgs1 = canonicalize_image(imgs1)
@@ -120,8 +127,16 @@ def ssim_fwd_bwd(ssims, dL_dimgs1, imgs1, imgs2, N_dssims_dQMP, should_zero: boo
         flags |= nat.USE_DSSIM
         if divide_by_two_in_dssim:
             flags |= nat.DIVIDE_BY_TWO
+    if grad_scale is not None and not skip_backward:
+        if tuple(grad_scale.shape) not in ((b,), ()) or (grad_scale.ndim == 0 and b != 1):
+            raise nat.DimensionMismatch(
+                f"Expected the gradient scale to have one entry per image ({b}); "
+                f"received size {tuple(grad_scale.shape)}.")
+        grad_scale = grad_scale.reshape(b).contiguous()
+    else:
+        grad_scale = None
     for name, t in (("imgs1", imgs1), ("imgs2", imgs2), ("ssims", None if skip_ssim else ssims),
-                    ("dL_dimgs1", dl_c)):
+                    ("dL_dimgs1", dl_c), ("grad_scale", grad_scale)):
         if t is not None:
             _require_device_array(name, t)
             if t.device != device:
@@ -131,13 +146,18 @@ def ssim_fwd_bwd(ssims, dL_dimgs1, imgs1, imgs2, N_dssims_dQMP, should_zero: boo
         stream = torch.cuda.current_stream(device)
         nbytes = nat.workspace_size(c, h, w, b, flags)
         ws = _workspace(device, stream, nbytes)
-        nat.fwd_bwd(
-            ssims.data_ptr() if not skip_ssim else 0, dtype_code(ssims) if not skip_ssim else nat.FLOAT32,
-            b if skip_ssim else int(ssims.shape[0]),
-            dl_c.data_ptr() if dl_c is not None else 0, dtype_code(dl_c) if dl_c is not None else nat.FLOAT32,
-            cimgs1.data_ptr(), dtype_code(cimgs1), cimgs2.data_ptr(), dtype_code(cimgs2), 0,
-            c, h, w, b, flags, ws.data_ptr() if ws is not None else 0,
-            ws.numel() if ws is not None else 0, stream.cuda_stream)
+        out_args = (ssims.data_ptr() if not skip_ssim else 0, dtype_code(ssims) if not skip_ssim else nat.FLOAT32,
+                    b if skip_ssim else int(ssims.shape[0]),
+                    dl_c.data_ptr() if dl_c is not None else 0,
+                    dtype_code(dl_c) if dl_c is not None else nat.FLOAT32,
+                    cimgs1.data_ptr(), dtype_code(cimgs1), cimgs2.data_ptr(), dtype_code(cimgs2))
+        ws_args = (ws.data_ptr() if ws is not None else 0, ws.numel() if ws is not None else 0,
+                   stream.cuda_stream)
+        if grad_scale is None:
+            nat.fwd_bwd(*out_args, 0, c, h, w, b, flags, *ws_args)
+        else:
+            nat.fwd_bwd_scaled(*out_args, c, h, w, b, flags, grad_scale.data_ptr(), dtype_code(grad_scale),
+                               *ws_args)
 
     if not skip_ssim and allocated_ssims and should_unpack(ssims, imgs1):
         ssims = ssims.item()           # the reference's blocking scalar read

@@ -98,9 +98,6 @@ KInfo kernel_info_s(int nt, bool /*fused*/, bool /*want_ssim*/)
     return kinfo<128, S, false, true, IO>();
 }
 
-#ifndef FSSIM_F32_STEP
-#define FSSIM_F32_STEP 8
-#endif
 template <bool F, bool WS>
 KInfo finfo()
 {
@@ -120,7 +117,7 @@ KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io, int iom)
             default: return pinfo_io<fssim::IN_ANY>(nt, want_ssim);
         }
     }
-    return f32io ? kernel_info_s<FSSIM_F32_STEP, true>(nt, fused, want_ssim)
+    return f32io ? kernel_info_s<8, true>(nt, fused, want_ssim)
                  : kernel_info_s<8, false>(nt, fused, want_ssim);
 }
 
@@ -203,9 +200,10 @@ int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f
     }
     // Gradient kernels: bands of 54 or 86 rows; forward only: 64, 96 or 128 rows.
     const int cands_fused[2] = {64, 96};
+    const int nfused = 2;
     const int cands_fwd[3] = {64, 96, 128};
     const int* cands = g.fused ? cands_fused : cands_fwd;
-    const int ncand = g.fused ? 2 : 3;
+    const int ncand = g.fused ? nfused : 3;
     int64_t best = -1;
     for (int ci = 0; ci < ncand; ++ci) {
         const int nt = cands[ci];
@@ -303,10 +301,14 @@ int fssim_workspace_size(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t fl
     return ok();
 }
 
-int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs1, int grad_dtype,
-                  const void* imgs1, int imgs1_dtype, const void* imgs2, int imgs2_dtype, void* qmp,
-                  int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, void* workspace,
-                  size_t workspace_bytes, void* stream)
+}  // extern "C"
+
+namespace {
+
+int fwd_bwd_impl(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs1, int grad_dtype,
+                 const void* imgs1, int imgs1_dtype, const void* imgs2, int imgs2_dtype, void* qmp, int64_t c,
+                 int64_t h, int64_t w, int64_t n, uint32_t flags, void* workspace, size_t workspace_bytes,
+                 void* stream, const void* grad_scale, int grad_scale_dtype)
 {
     (void)qmp;   // the partial gradients never leave the chip (see fastssim.h)
     const uint32_t known = FSSIM_SKIP_SSIM | FSSIM_SKIP_BACKWARD | FSSIM_USE_DSSIM | FSSIM_DIVIDE_BY_TWO |
@@ -398,12 +400,43 @@ int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimg
     // DSSIM sign (src/core.jl:648) is folded in here.
     const double scale = ((p.use_dssim && p.div2) ? 0.5 : 1.0) / p.npx;
     p.gscale = static_cast<float>(p.use_dssim ? -scale : scale);
+    p.img_scale = grad_scale;
+    p.isdt = grad_scale_dtype;
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     void* args[] = {&p};
     cudaError_t e = cudaLaunchKernel(g.ki.fn, dim3(static_cast<unsigned>(g.grid)), dim3(g.ki.threads), args, g.ki.smem, s);
     if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
     return ok();
+}
+
+}  // namespace
+
+extern "C" {
+
+int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs1, int grad_dtype,
+                  const void* imgs1, int imgs1_dtype, const void* imgs2, int imgs2_dtype, void* qmp,
+                  int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, void* workspace,
+                  size_t workspace_bytes, void* stream)
+{
+    return fwd_bwd_impl(ssims, ssims_dtype, ssims_len, dL_dimgs1, grad_dtype, imgs1, imgs1_dtype, imgs2,
+                        imgs2_dtype, qmp, c, h, w, n, flags, workspace, workspace_bytes, stream, nullptr, 0);
+}
+
+int fssim_fwd_bwd_scaled(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs1, int grad_dtype,
+                         const void* imgs1, int imgs1_dtype, const void* imgs2, int imgs2_dtype, int64_t c,
+                         int64_t h, int64_t w, int64_t n, uint32_t flags, const void* grad_scale,
+                         int grad_scale_dtype, void* workspace, size_t workspace_bytes, void* stream)
+{
+    if (!grad_scale) return fail(FSSIM_ERR_INVALID_ARGUMENT, "grad_scale must not be NULL");
+    if (!is_float_dtype(grad_scale_dtype))
+        return fail(FSSIM_ERR_UNSUPPORTED_DTYPE, "grad_scale dtype must be FLOAT32, FLOAT64 or FLOAT16 (got %d)",
+                    grad_scale_dtype);
+    if (!aligned(grad_scale, dsize(grad_scale_dtype)))
+        return fail(FSSIM_ERR_MISALIGNED, "grad_scale must be aligned to its element size");
+    return fwd_bwd_impl(ssims, ssims_dtype, ssims_len, dL_dimgs1, grad_dtype, imgs1, imgs1_dtype, imgs2,
+                        imgs2_dtype, nullptr, c, h, w, n, flags, workspace, workspace_bytes, stream, grad_scale,
+                        grad_scale_dtype);
 }
 
 }  // extern "C"

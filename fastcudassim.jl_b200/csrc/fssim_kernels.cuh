@@ -67,6 +67,8 @@ struct Params {
     float C1, C2;             // src/core.jl:49-50
     float gscale;             // +-1/N or +-0.5/N (src/core.jl:584-589, sign for DSSIM)
     double npx;               // N = C*H*W as a double
+    const void* img_scale;    // optional per-image gradient factor (length N), dtype isdt
+    int isdt;
 };
 
 __device__ __forceinline__ float rcp_approx(float v)
@@ -599,10 +601,6 @@ namespace fssim {
 // Unrolling further (5 slots, to index 40-column rings at compile time) was
 // measured slower: the larger body misses the instruction cache.
 // ---------------------------------------------------------------------------
-// Which group stages the x/y values B2 needs (0: group A, 1: group B).
-#ifndef FSSIM_XY_IN_B
-#define FSSIM_XY_IN_B 0
-#endif
 
 template <int NT>
 struct PGeo {
@@ -676,6 +674,9 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
     const uint32_t CH32 = static_cast<uint32_t>(C) * static_cast<uint32_t>(H);
     const int ns = (Lc + 2 * LAG - 1) / S + 1;
     const int nslot = (ns + G::LATENCY + 1) & ~1;   // even: group B runs two slots per iteration
+    // +-1/N (or +-0.5/N), times the image's factor when one is given; doubled for inv2
+    const float gscale2 =
+        2.f * (p.img_scale ? static_cast<float>(p.gscale * ld_out(p.img_scale, p.isdt, n)) : p.gscale);
 
     float2 KP[RAD + 1];
 #pragma unroll
@@ -803,9 +804,7 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
             const bool next_xy = t >= 2 && t - 2 < ns;
             if (F32IO) {
                 if (next_stage) issue_stage(t + 1, stage + ((t + 1) & 1) * STG);
-#if !FSSIM_XY_IN_B
                 if (next_xy) issue_xy(t - 2, xyb + ((t + 1) & 1) * XYN);
-#endif
                 cp_async_commit();
             } else {
                 if (next_stage) load_stage_raw(t + 1);
@@ -900,25 +899,8 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
         TA[0] = TA[1] = TB[0] = TB[1] = TQ[0] = TQ[1] = make_float2(0.f, 0.f);
         TP[0] = TP[1] = 0.f;
 
-#if FSSIM_XY_IN_B
-        auto issue_xy_b = [&](int k, float2* buf) {    // xyb <- x, y at this row's gradient pixels of step k
-            const int cb = w0 - LAG + k * S - 2 * RAD;
-#pragma unroll
-            for (int o = 0; o < S; ++o) {
-                const int wc = cb + o;
-                const bool ok = grow_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc);
-                const uint32_t off = grow_off + CH32 * static_cast<uint32_t>(ok ? wc : 0);
-                cp_async4(&buf[tb * SP + o].x, xg + off, ok);
-                cp_async4(&buf[tb * SP + o].y, yg + off, ok);
-            }
-            cp_async_commit();
-        };
-#endif
         auto bslot = [&](int t, float2(&Acur)[S], float2(&Aprv)[S], float2(&Bcur)[S], float2(&Bprv)[S],
                          float2(&Qcur)[S], float2(&Qprv)[S], float(&Pcur)[S], float(&Pprv)[S]) {
-#if FSSIM_XY_IN_B
-            if (t >= 2 && t - 2 < ns) issue_xy_b(t - 2, xyb + ((t + 1) & 1) * XYN);
-#endif
             // Both stages run in every slot (so the history blocks are written
             // unconditionally and never held live twice); outside the stream they read
             // stale or zeroed buffers, and nothing they produce there is stored or owned.
@@ -963,7 +945,7 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
                     // dS/dQ = -s/t, dS/dM = 2/(zt) ((by-ax) my + s (z-t) mx), dS/dP = 2 ax/(zt)
                     // (src/core.jl:384-388), times +-1/N, zero outside the image, dQ doubled.
                     const bool in_img = row_in && static_cast<unsigned>(wc) < static_cast<unsigned>(W);
-                    const float inv2 = in_img ? 2.f * p.gscale * inv : 0.f;
+                    const float inv2 = in_img ? gscale2 * inv : 0.f;
                     const float dq2 = -(s * z) * inv2;
                     const float dm = inv2 * fmaf(by - ax, my, (s * (z - tt)) * mx);
                     const float dp = ax * inv2;
@@ -1016,9 +998,6 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
                 TP[0] = Pprv[S - 2];
                 TP[1] = Pprv[S - 1];
             }
-#if FSSIM_XY_IN_B
-            cp_async_wait<0>();
-#endif
             __syncthreads();
         };
 
@@ -1136,7 +1115,8 @@ __global__ void __launch_bounds__(D64Geo::NT) f64_kernel(const Params p)
     __syncthreads();
     // w-direction pass, SSIM map (own pixels), partials on the TP x TP tile
     const double gscale = static_cast<double>(p.use_dssim ? -1.0 : 1.0) *
-                          ((p.use_dssim && p.div2) ? 0.5 : 1.0) / p.npx;
+                          ((p.use_dssim && p.div2) ? 0.5 : 1.0) / p.npx *
+                          (p.img_scale ? ld_out(p.img_scale, p.isdt, n) : 1.0);
     double tsum = 0.0;
     for (int e = tid; e < TP * TP; e += NT) {
         const int r = e % TP, q = e / TP;        // partial pixel (r, q) <-> image (h0-R+r, w0-R+q)

@@ -113,6 +113,25 @@ int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len,
                   void* stream);
 
 /*
+ * fssim_fwd_bwd_scaled - fssim_fwd_bwd with a per-image factor on the gradient:
+ * dL_dimgs1[:, :, :, i] = grad_scale[i] * d(D)SSIM_i / dimgs1.  Replaces the
+ * pullback's separate broadcast `dL_dimgs1 .*= reshape(dL_dssims, 1, 1, 1, :)`
+ * of the reference's rrules (ext/FastCUDASSIMChainRulesCoreExt.jl:28-36, :63-68)
+ * when the gradient is computed at pullback time, with the cotangent known.
+ * grad_scale: length-n device vector (FLOAT32, FLOAT64 or FLOAT16).  Other
+ * arguments as fssim_fwd_bwd (without qmp); the (D)SSIM values are not scaled.
+ */
+int fssim_fwd_bwd_scaled(void* ssims, int ssims_dtype, int64_t ssims_len,
+                         void* dL_dimgs1, int grad_dtype,
+                         const void* imgs1, int imgs1_dtype,
+                         const void* imgs2, int imgs2_dtype,
+                         int64_t c, int64_t h, int64_t w, int64_t n,
+                         uint32_t flags,
+                         const void* grad_scale, int grad_scale_dtype,
+                         void* workspace, size_t workspace_bytes,
+                         void* stream);
+
+/*
  * fssim_fwd_bwd_noalloc - fssim_fwd_bwd for callers that cannot allocate device memory.
  *
  * No counterpart in the reference: FastCUDASSIM.jl allocates its own buffers

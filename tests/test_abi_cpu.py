@@ -60,3 +60,22 @@ def test_nothing_requested_is_a_no_op(pkg):
     st = lib.fssim_fwd_bwd(None, 0, 1, None, 0, ctypes.c_void_p(16), 0, ctypes.c_void_p(16), 0, None,
                            3, 8, 8, 2, flags, None, 0, None)
     assert st == pkg._native.OK
+
+
+def test_scaled_entry_point_argument_errors(pkg):
+    lib = pkg._native.load()
+    nat = pkg._native
+    x = ctypes.c_void_p(16)
+    # a missing factor vector, a factor vector of a non-float type, a misaligned one
+    st = lib.fssim_fwd_bwd_scaled(None, 0, 1, x, 0, x, 0, x, 0, 1, 8, 8, 1, nat.SKIP_SSIM, None, 0, None, 0, None)
+    assert st == nat.ERR_INVALID_ARGUMENT
+    st = lib.fssim_fwd_bwd_scaled(None, 0, 1, x, 0, x, 0, x, 0, 1, 8, 8, 1, nat.SKIP_SSIM, x, nat.N0F8,
+                                  None, 0, None)
+    assert st == nat.ERR_UNSUPPORTED_DTYPE
+    st = lib.fssim_fwd_bwd_scaled(None, 0, 1, x, 0, x, 0, x, 0, 1, 8, 8, 1, nat.SKIP_SSIM, ctypes.c_void_p(18),
+                                  nat.FLOAT32, None, 0, None)
+    assert st == nat.ERR_MISALIGNED
+    # the remaining checks are those of fssim_fwd_bwd
+    st = lib.fssim_fwd_bwd_scaled(None, 0, 1, x, 0, x, 0, x, 0, 0, 8, 8, 1, nat.SKIP_SSIM, x, nat.FLOAT32,
+                                  None, 0, None)
+    assert st == nat.ERR_INVALID_ARGUMENT
