@@ -107,6 +107,23 @@ class ClockSampler:
                 "reasons": sorted(reasons), "samples": len(sms)}
 
 
+# FP32 FMA-equivalents per element of the fused kernel, counted with ncu
+# (sass__inst_executed_per_opcode: FFMA2/FADD2/FMUL2 count 2, FFMA/FADD/FMUL 1).
+FMA_PER_ELEM = 221
+
+
+def fp32_pipe(kern_s, n_local, clocks, sms):
+    """The binding roof of the fused kernel: FP32 FMA pipe use against 128 lanes per SM
+    per clock at the SM clock sampled during the timed region."""
+    mhz = clocks.get("sm_mhz") or clocks.get("sm_max_mhz")
+    if not mhz:
+        return None
+    achieved = FMA_PER_ELEM * n_local * C * H * W / kern_s / 1e12
+    peak = sms * 128 * mhz * 1e6 / 1e12
+    return {"fma_per_elem": FMA_PER_ELEM, "achieved_tfma_s": achieved, "peak_tfma_s": peak,
+            "frac": achieved / peak, "clock_mhz": mhz}
+
+
 def cpu_oracle_rate(n_images, nthreads, reps=1):
     """Gpixel/s of the oracle (reference algorithm, single precision) on host cores."""
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
@@ -232,14 +249,29 @@ def run_ours(args):
         hs = torch.empty(N_IMAGES, dtype=torch.float32, pin_memory=True)
         dx = pkg.jl_empty((C, H, W, n_local), torch.float32, dev)
         dy = pkg.jl_empty((C, H, W, n_local), torch.float32, dev)
-        dxf = dx.permute(3, 2, 1, 0).reshape(-1)
+        dxf = dx.permute(3, 2, 1, 0).reshape(-1)      # memory order: image n at [n*E, (n+1)*E)
         dyf = dy.permute(3, 2, 1, 0).reshape(-1)
         e2e_steps = max(1, min(args.steps, 3))
+        # The host-to-device copies run on their own stream in chunks of images, and each
+        # chunk's call starts once its copy has landed, so the copies overlap the kernels.
+        copy_stream = torch.cuda.Stream(dev)
+        n_chunks = min(16, n_local)
+        bounds = [(n_local * j // n_chunks, n_local * (j + 1) // n_chunks) for j in range(n_chunks)]
+        E = C * H * W
+        landed = [torch.cuda.Event() for _ in bounds]
 
         def e2e_step():
-            dxf.copy_(hx, non_blocking=True)
-            dyf.copy_(hy, non_blocking=True)
-            pkg.ssim_with_gradient_(ssims, grad, dx, dy, None, True)
+            start = torch.cuda.Event()
+            start.record(stream)                     # the previous step's calls are done with dx, dy
+            copy_stream.wait_event(start)
+            for (lo_i, hi_i), ev in zip(bounds, landed):
+                with torch.cuda.stream(copy_stream):
+                    dxf[lo_i * E:hi_i * E].copy_(hx[lo_i * E:hi_i * E], non_blocking=True)
+                    dyf[lo_i * E:hi_i * E].copy_(hy[lo_i * E:hi_i * E], non_blocking=True)
+                    ev.record(copy_stream)
+                stream.wait_event(ev)
+                pkg.ssim_with_gradient_(ssims[lo_i:hi_i], grad[..., lo_i:hi_i], dx[..., lo_i:hi_i],
+                                        dy[..., lo_i:hi_i], None, True)
             scores = sharded.gather_scores(ssims, N_IMAGES) if world > 1 else ssims
             hs.copy_(scores, non_blocking=True)
 
@@ -256,7 +288,8 @@ def run_ours(args):
             dist.all_reduce(te, op=dist.ReduceOp.MAX)
         e2e = {"value": e2e_steps * N_IMAGES * H * W / float(te[0]) / 1e9, "unit": "Gpixel/s",
                "h2d_bytes_per_step": int(2 * n_local * C * H * W * 4), "d2h_bytes_per_step": int(N_IMAGES * 4),
-               "steps": e2e_steps}
+               "steps": e2e_steps, "calls_per_step": n_chunks,
+               "overlap": "pinned host buffers; H2D in image chunks on a copy stream, overlapped with the calls"}
         del hx, hy, dx, dy, dxf, dyf
 
     extras = {}
@@ -274,6 +307,7 @@ def run_ours(args):
         dist.destroy_process_group()
     if rank != 0:
         return 0
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
     peak, peak_kind = measured_peaks()
     pixels = N_IMAGES * H * W
     value = args.steps * pixels / elapsed / 1e9
@@ -292,6 +326,7 @@ def run_ours(args):
                      "traffic": traffic_per_launch(n_local),
                      "kernel": "fssim::pipe_kernel<96,true>", "kernel_ms": kern * 1e3,
                      "alg_bytes_per_launch": alg_bytes},
+        "fp32_pipe": fp32_pipe(kern, n_local, clocks, sms),
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": args.steps,
@@ -315,6 +350,9 @@ def side_benchmarks(pkg, dev):
         ts = []
         for i in range(reps + 3):
             flush.zero_()
+            # keep the device busy while the host enqueues the call, so the events
+            # bracket device work only (the Python call itself takes tens of us)
+            torch.cuda._sleep(2_000_000)
             a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             a.record()
             fn()
@@ -378,9 +416,10 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
-    ap.add_argument("--profile-case", choices=["fused", "fwd", "fused_u8", "fused_f16"], default=None,
-                    help="only run the kernel on 64x3x512x512 f32 (a size for ncu captures): "
-                         "warmup + steps launches, no timing output")
+    ap.add_argument("--profile-case", choices=["fused", "fwd", "fused_u8", "fused_f16", "fhd1", "fhd3"],
+                    default=None,
+                    help="only run one kernel on a small case (a size for ncu captures): "
+                         "warmup + steps launches and their mean time")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -392,15 +431,16 @@ def main():
 
 
 def profile_case(args):
-    """warmup + steps launches of one kernel on 64x3x512x512 f32 (0.3 GB, larger than L2)."""
+    """warmup + steps launches of one kernel: on 64x3x512x512 (0.3 GB in Float32, larger than
+    L2) for the batch cases, on one 1x1080x1920 or 3x1080x1920 image for the full-HD cases."""
     import torch
     import __graft_entry__ as ge
     pkg = ge.load_package()
     syn = __import__(pkg.__name__ + ".synthetic", fromlist=["x"])
-    shape = (C, H, W, 64)
+    shape = {"fhd1": (1, 1080, 1920, 1), "fhd3": (3, 1080, 1920, 1)}.get(args.profile_case, (C, H, W, 64))
     dt = {"fused_u8": torch.uint8, "fused_f16": torch.float16}.get(args.profile_case, torch.float32)
     x, y = syn.device_pair(shape, NOISE, dtype=dt)
-    s = torch.empty(64, dtype=torch.float32, device="cuda")
+    s = torch.empty(shape[3], dtype=torch.float32, device="cuda")
     g = pkg.jl_empty(shape, torch.float32)
     def launch():
         if args.profile_case.startswith("fused"):
@@ -417,7 +457,7 @@ def profile_case(args):
     torch.cuda.synchronize()
     ms = a.elapsed_time(b) / max(args.steps, 1)
     print(json.dumps({"profile_case": args.profile_case, "launches": args.warmup + args.steps,
-                      "ms_per_launch": ms, "gelem_per_s": 64 * C * H * W / ms / 1e6, "ssim0": float(s[0])}))
+                      "ms_per_launch": ms, "gelem_per_s": x.numel() / ms / 1e6, "ssim0": float(s[0])}))
     return 0
 
 
