@@ -67,13 +67,12 @@ struct KInfo {
     int threads;   // CTA size
 };
 
-// Kernel variants: band height NT (threads), step width S (columns), with or
-// without the gradient, with or without the SSIM reduction, Float32 I/O or not.
-template <int NT, int S, bool F, bool WS, bool IO>
+// Forward streaming kernel (Float32 inputs): band height NT (threads).
+template <int NT>
 KInfo kinfo()
 {
-    return KInfo{reinterpret_cast<const void*>(&fssim::band_kernel<NT, S, F, WS, IO>),
-                 fssim::Geo<NT, S, F, IO>::total, NT, S, NT};
+    return KInfo{reinterpret_cast<const void*>(&fssim::band_kernel<NT>), fssim::Geo<NT>::total, NT,
+                 fssim::Geo<NT>::S, NT};
 }
 
 template <int NT, bool WS, int IOM>
@@ -90,12 +89,33 @@ KInfo pinfo_io(int nt, bool want_ssim)
     return want_ssim ? pinfo<96, true, IOM>() : pinfo<96, false, IOM>();
 }
 
-template <int S, bool IO>
-KInfo kernel_info_s(int nt, bool /*fused*/, bool /*want_ssim*/)
+template <int IM>
+KInfo tinfo()
 {
-    if (nt == 64) return kinfo<64, S, false, true, IO>();
-    if (nt == 96) return kinfo<96, S, false, true, IO>();
-    return kinfo<128, S, false, true, IO>();
+    return KInfo{reinterpret_cast<const void*>(&fssim::tile_fwd_kernel<IM>), fssim::TGeo::total, fssim::TGeo::TH,
+                 fssim::TGeo::TW, fssim::TGeo::NT};
+}
+
+KInfo tile_info(bool f32io, int iom)
+{
+    if (f32io) return tinfo<0>();
+    if (iom == fssim::IN_U8) return tinfo<fssim::IN_U8>();
+    if (iom == fssim::IN_F16) return tinfo<fssim::IN_F16>();
+    return tinfo<fssim::IN_ANY>();
+}
+
+// Forward-only calls on the tile kernel: converted (N0f8 / Float16 / mixed)
+// inputs at every size, since the streaming kernel converting in the loader
+// needed about 200 registers a thread; Float32 inputs up to 4 Mi elements,
+// where a streaming grid needs many short segments (halo warm-up, two warps
+// per CTA).  Measured on B200 (us, tile vs streaming): 1x1080x1920 F32 26.6 vs
+// 30.7, 3x1080x1920 F32 63.5 vs 59.4, 3x1080x1920 N0f8 65.5 vs 85.5,
+// 64x3x512x512 F32 431 vs 324, 64x3x512x512 N0f8 442 vs 545.
+constexpr int64_t kTileMaxF32Elems = int64_t(1) << 22;
+
+bool use_tiles(int64_t c, int64_t h, int64_t w, int64_t n, bool f32io)
+{
+    return !f32io || c * h * w * n <= kTileMaxF32Elems;
 }
 
 template <bool F, bool WS>
@@ -106,7 +126,8 @@ KInfo finfo()
 }
 
 // Gradients run the two-group pipelined kernel (32-bit in-image offsets: the
-// caller guarantees C*H*W < 2^31); forward-only SSIM runs the single-group kernel.
+// caller guarantees C*H*W < 2^31); forward-only SSIM on Float32 inputs runs the
+// single-group streaming kernel (or tiles, see use_tiles).
 KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io, int iom)
 {
     if (fused) {
@@ -117,8 +138,10 @@ KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io, int iom)
             default: return pinfo_io<fssim::IN_ANY>(nt, want_ssim);
         }
     }
-    return f32io ? kernel_info_s<8, true>(nt, fused, want_ssim)
-                 : kernel_info_s<8, false>(nt, fused, want_ssim);
+    (void)f32io;   // converted inputs run forward-only as tiles (see use_tiles)
+    if (nt == 64) return kinfo<64>();
+    if (nt == 96) return kinfo<96>();
+    return kinfo<128>();
 }
 
 // Per-device facts, computed once per (device, kernel) under a lock.
@@ -195,6 +218,23 @@ int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f
         g.grid = n * g.cpi;
         g.ws_counters = ((static_cast<size_t>(n) * sizeof(unsigned) + 255) / 256) * 256;
         g.ws_bytes = g.want_ssim ? g.ws_counters + static_cast<size_t>(n) * g.cpi * sizeof(double) : 0;
+        *cfg = g;
+        return FSSIM_OK;
+    }
+    if (!g.fused && use_tiles(c, h, w, n, f32io)) {   // small forward-only call: one TH x TW tile per CTA
+        g.ki = tile_info(f32io, iom);
+        int sms = 0, occ = 0;
+        int st = device_facts(g.ki, &sms, &occ);
+        if (st != FSSIM_OK) return st;
+        g.nt = fssim::TGeo::TH;
+        g.T = fssim::TGeo::TH;
+        g.nb = static_cast<int>(cdiv(h, fssim::TGeo::TH));
+        g.nseg = static_cast<int>(cdiv(w, fssim::TGeo::TW));
+        g.L = fssim::TGeo::TW;
+        g.cpi = c * g.nb * g.nseg;
+        g.grid = n * g.cpi;   // one tile per CTA
+        g.ws_counters = ((static_cast<size_t>(n) * sizeof(unsigned) + 255) / 256) * 256;
+        g.ws_bytes = g.ws_counters + static_cast<size_t>(n) * g.cpi * sizeof(double);
         *cfg = g;
         return FSSIM_OK;
     }
@@ -352,15 +392,14 @@ int fwd_bwd_impl(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs
                     (long long)(c * h * w));
     const bool f32io = imgs1_dtype == FSSIM_FLOAT32 && imgs2_dtype == FSSIM_FLOAT32 &&
                        (!fused || grad_dtype == FSSIM_FLOAT32);
-    const int iom = (imgs1_dtype == FSSIM_N0F8 && imgs2_dtype == FSSIM_N0F8 && grad_dtype == FSSIM_FLOAT32)
-                        ? fssim::IN_U8
-                    : (imgs1_dtype == FSSIM_FLOAT16 && imgs2_dtype == FSSIM_FLOAT16 && grad_dtype == FSSIM_FLOAT32)
-                        ? fssim::IN_F16
-                        : fssim::IN_ANY;
+    const bool f32grad = !fused || grad_dtype == FSSIM_FLOAT32;
+    const int iom = (imgs1_dtype == FSSIM_N0F8 && imgs2_dtype == FSSIM_N0F8 && f32grad)        ? fssim::IN_U8
+                    : (imgs1_dtype == FSSIM_FLOAT16 && imgs2_dtype == FSSIM_FLOAT16 && f32grad) ? fssim::IN_F16
+                                                                                             : fssim::IN_ANY;
     // Float64 on either input: compute in double (promote_type(T1, T2, Float32), src/core.jl:953-954)
     const bool f64 = imgs1_dtype == FSSIM_FLOAT64 || imgs2_dtype == FSSIM_FLOAT64;
     Cfg g;
-    st = configure(c, h, w, n, flags, f32io && !f64, f64 ? IOM_F64 : (fused ? iom : fssim::IN_ANY), &g);
+    st = configure(c, h, w, n, flags, f32io && !f64, f64 ? IOM_F64 : iom, &g);
     if (st != FSSIM_OK) return st;
     if (want_ssim) {
         if (!workspace || workspace_bytes < g.ws_bytes)

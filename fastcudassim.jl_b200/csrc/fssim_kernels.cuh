@@ -9,9 +9,9 @@
 // columns [w0, w0+L) along the width axis.  It streams along the width axis in
 // steps of S columns:
 //
-//   loader  global (C,H,W,N) -> shared staging, two steps ahead with cp.async
-//           (Float32 I/O) or one step ahead through registers with an in-kernel
-//           conversion (Float16, N0f8 inputs; Float16 / Float64 gradients)
+//   loader  global (C,H,W,N) -> shared staging with cp.async (Float32 I/O), or
+//           one step ahead through registers with an in-kernel conversion
+//           (Float16, N0f8 inputs; Float16 / Float64 gradients)
 //   F1      h-direction 11-tap Gaussian of the 4 moment images x, y, x^2+y^2, xy
 //           (each thread: V = 8 consecutive rows of one column; taps from smem)
 //   F2      w-direction 11-tap Gaussian (each thread: one row; the 10 previous
@@ -26,6 +26,10 @@
 // backward correlation needs partials there); the width halo costs nothing but
 // the 10+10 warm-up columns of each segment.  Nothing but the inputs, the
 // gradient and one double per CTA ever touches global memory.
+//
+// Kernels: pipe_kernel (SSIM + gradient, two warp groups), band_kernel (forward
+// only, Float32 inputs), tile_fwd_kernel (forward only: small Float32 calls and
+// converted inputs), f64_kernel (any call with a Float64 input).
 //
 // Only four moment images are convolved, not the reference's five: the SSIM map
 // needs the two variances only through their sum, so E[x^2] and E[y^2] are
@@ -164,32 +168,27 @@ __device__ __forceinline__ void cp_async_wait()
     asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
 }
 
-// Geometry and shared-memory footprint of one CTA (host and device agree on it).
-template <int NT, int S, bool FUSED, bool F32IO>
+// Geometry and shared-memory footprint of one CTA of the forward streaming
+// kernel (host and device agree on it).
+template <int NT>
 struct Geo {
-    static constexpr int R1 = NT;                          // moment / partial rows
-    static constexpr int T = FUSED ? NT - 2 * RAD : NT;    // output rows of a band
+    static constexpr int S = 8;                            // columns per step
+    static constexpr int R1 = NT;                          // moment rows = output rows of a band
+    static constexpr int T = NT;
     static constexpr int R2 = R1 + 2 * RAD;                // input rows
-    static constexpr int LAG = FUSED ? 2 * RAD : RAD;      // input row/column offset of the stream
+    static constexpr int LAG = RAD;                        // input column offset of the stream
     static constexpr int SP = S + 1;                       // staging row stride (float2), odd
     static constexpr int FC = S + 1;                       // float4 row stride, odd: conflict-free
     static constexpr int NRUN1 = R1 / V;                   // F1 runs per column
     static constexpr int IT1 = S * NRUN1 / NT;             // F1 items per thread
-    static constexpr int NRUNB = (T + V - 1) / V;          // B1 runs per column
-    static constexpr int ITB = (S * NRUNB + NT - 1) / NT;  // B1 items per thread (last round partial)
-    static constexpr int QROWS = NRUNB * V + 2 * RAD;      // partial rows incl. zero padding
-    static constexpr int LROWS = (R2 + NT - 1) / NT;       // staging rows per thread (cp.async loader)
-    static constexpr int NLOAD = (R2 * S + NT - 1) / NT;   // staged elements per thread (register loader)
+    static constexpr int LROWS = (R2 + NT - 1) / NT;       // staging rows per thread
     static constexpr int stage_one = R2 * SP * 8;
-    static constexpr int stage_bytes = (F32IO ? 2 : 1) * stage_one;
+    static constexpr int stage_bytes = 2 * stage_one;
     static constexpr int f1_bytes = R1 * FC * 16;
-    static constexpr int qmp_bytes = FUSED ? QROWS * FC * 16 : 0;
-    static constexpr int b1_bytes = FUSED ? NT * FC * 16 : 0;
     static constexpr int red_bytes = (NT / 32 + 2) * 8;
-    static constexpr int total = stage_bytes + f1_bytes + qmp_bytes + b1_bytes + red_bytes;
+    static constexpr int total = stage_bytes + f1_bytes + red_bytes;
     static_assert(R1 % V == 0 && NT % 32 == 0, "band geometry");
     static_assert((S * NRUN1) % NT == 0, "F1 items must divide evenly over the CTA");
-    static_assert(NRUNB * V <= NT, "B1 rows must fit the B2 buffer");
     static_assert(stage_one % 16 == 0, "staging must keep 16-byte alignment");
 };
 
@@ -222,38 +221,36 @@ __device__ __forceinline__ void finish_image(const Params& p, int n, int local_c
         red[NT / 32] = (prev == static_cast<unsigned>(p.cpi - 1)) ? 1.0 : 0.0;
     }
     __syncthreads();
-    if (red[NT / 32] == 0.0) return;
-    __threadfence();
-    double v = 0.0;
-    for (int i = threadIdx.x; i < p.cpi; i += NT) v += __ldcg(&p.partials[(int64_t)n * p.cpi + i]);
-    __syncthreads();   // red[] is reused below
-    const double sum = block_sum<NT>(v, red);
-    if (threadIdx.x == 0) {
-        double s = sum;
-        if (!p.should_zero) s += ld_out(p.ssims, p.sdt, n);
-        s = s / p.npx;                               // src/core.jl:1125-1157
-        if (p.use_dssim) s = p.div2 ? (1.0 - s) * 0.5 : 1.0 - s;
-        st_out(p.ssims, p.sdt, n, s);
-        p.counters[n] = 0u;                          // leave the workspace zeroed
+    if (red[NT / 32] != 0.0) {   // uniform over the CTA; no early return, so loops may call this
+        __threadfence();
+        double v = 0.0;
+        for (int i = threadIdx.x; i < p.cpi; i += NT) v += __ldcg(&p.partials[(int64_t)n * p.cpi + i]);
+        __syncthreads();   // red[] is reused below
+        const double sum = block_sum<NT>(v, red);
+        if (threadIdx.x == 0) {
+            double s = sum;
+            if (!p.should_zero) s += ld_out(p.ssims, p.sdt, n);
+            s = s / p.npx;                               // src/core.jl:1125-1157
+            if (p.use_dssim) s = p.div2 ? (1.0 - s) * 0.5 : 1.0 - s;
+            st_out(p.ssims, p.sdt, n, s);
+            p.counters[n] = 0u;                          // leave the workspace zeroed
+        }
     }
 }
 
-// F32IO: both inputs and the gradient are Float32 - loads go straight to shared
-// memory with cp.async (double-buffered, two steps ahead) and no conversion;
-// otherwise elements are loaded by type, converted, and staged through registers.
-template <int NT, int S, bool FUSED, bool WANT_SSIM, bool F32IO>
-__global__ void __launch_bounds__(NT, (FUSED || !F32IO) ? 2 : 3) band_kernel(const Params p)
+// Forward-only streaming kernel for Float32 inputs (SSIM values, no gradient).
+// Loads go straight to shared memory with cp.async, double-buffered two steps
+// ahead; two barriers per step (after F1, after F2).
+template <int NT>
+__global__ void __launch_bounds__(NT, 3) band_kernel(const Params p)
 {
-    using G = Geo<NT, S, FUSED, F32IO>;
-    constexpr int R1 = G::R1, T = G::T, R2 = G::R2, LAG = G::LAG;
+    using G = Geo<NT>;
+    constexpr int S = G::S, T = G::T, R2 = G::R2, LAG = G::LAG;
     constexpr int SP = G::SP, FC = G::FC;
-    constexpr int NRUNB = G::NRUNB, QROWS = G::QROWS;
 
     extern __shared__ __align__(16) unsigned char smem_raw[];
     float2* stage = reinterpret_cast<float2*>(smem_raw);
     float4* f1buf = reinterpret_cast<float4*>(smem_raw + G::stage_bytes);
-    float4* qmp = reinterpret_cast<float4*>(smem_raw + G::stage_bytes + G::f1_bytes);
-    float4* b1buf = reinterpret_cast<float4*>(smem_raw + G::stage_bytes + G::f1_bytes + G::qmp_bytes);
     double* red = reinterpret_cast<double*>(smem_raw + G::total - G::red_bytes);
 
     const int tid = threadIdx.x;
@@ -271,8 +268,8 @@ __global__ void __launch_bounds__(NT, (FUSED || !F32IO) ? 2 : 3) band_kernel(con
     const int wend = min(w0 + p.L, W);
     const int Lc = wend - w0;
     const int64_t ibase = static_cast<int64_t>(n) * p.img_elems + c;
-    // Steps: the last owned output column (stream coordinate Lc-1+2*LAG-... ) must come
-    // out of the final step: ns = ceil((Lc + 2*LAG - S) / S) + 1.
+    // Steps: the last owned output column must come out of the final step:
+    // ns = ceil((Lc + 2*LAG - S) / S) + 1.
     const int ns = (Lc + 2 * LAG - 1) / S + 1;
 
     // Gaussian weights as (k, k) pairs for the packed FMAs.
@@ -280,14 +277,10 @@ __global__ void __launch_bounds__(NT, (FUSED || !F32IO) ? 2 : 3) band_kernel(con
 #pragma unroll
     for (int i = 0; i <= RAD; ++i) KP[i] = make_float2(p.kh[i], p.kh[i]);
 #define FSSIM_K2(tap) KP[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
-#define FSSIM_K1(tap) p.kh[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
 
-    if (FUSED)
-        for (int e = tid; e < (QROWS - R1) * FC; e += NT) qmp[R1 * FC + e] = make_float4(0.f, 0.f, 0.f, 0.f);
-
-    // ---------------- loaders: one step = S columns x R2 rows ----------------
-    // cp.async loader (F32IO): thread `tid` owns staging rows tid, tid+NT, ...
-    // and walks the S columns of the step; lanes cover consecutive rows.
+    // ---------------- loader: one step = S columns x R2 rows ----------------
+    // thread `tid` owns staging rows tid, tid+NT, ... and walks the S columns of
+    // the step; lanes cover consecutive rows.
     int64_t lrow_base[G::LROWS];
     bool lrow_ok[G::LROWS];
 #pragma unroll
@@ -316,65 +309,21 @@ __global__ void __launch_bounds__(NT, (FUSED || !F32IO) ? 2 : 3) band_kernel(con
         }
         cp_async_commit();
     };
-    // register loader (other dtypes): element e = tid + NT*u of the step.
-    uint32_t rx[F32IO ? 1 : G::NLOAD], ry[F32IO ? 1 : G::NLOAD];
-    auto issue_loads = [&](int k) {
-#pragma unroll
-        for (int u = 0; u < (F32IO ? 0 : G::NLOAD); ++u) {
-            const int e = tid + NT * u;
-            rx[u] = 0u;
-            ry[u] = 0u;
-            if (e < R2 * S) {
-                const int i = e % R2, j = e / R2;
-                const int hr = h0 - LAG + i;
-                const int wc = w0 - LAG + k * S + j;
-                if (k < ns && hr >= 0 && hr < H && wc >= 0 && wc < W) {
-                    const int64_t g = ibase + static_cast<int64_t>(C) * hr + CH * wc;
-                    rx[u] = ld_raw(p.x, p.xdt, g);
-                    ry[u] = ld_raw(p.y, p.ydt, g);
-                }
-            }
-        }
-    };
-    auto store_stage = [&]() {
-#pragma unroll
-        for (int u = 0; u < (F32IO ? 0 : G::NLOAD); ++u) {
-            const int e = tid + NT * u;
-            if (e < R2 * S) {
-                const int i = e % R2, j = e / R2;
-                stage[i * SP + j] = make_float2(cvt_raw(rx[u], p.xdt, nullptr), cvt_raw(ry[u], p.ydt, nullptr));
-            }
-        }
-    };
 
-    if (F32IO) {
-        issue_async(0, stage);
-        issue_async(1, stage + R2 * SP);
-        cp_async_wait<1>();
-    } else {
-        issue_loads(0);
-        store_stage();
-        issue_loads(1);
-    }
+    issue_async(0, stage);
+    issue_async(1, stage + R2 * SP);
+    cp_async_wait<1>();
     __syncthreads();
 
-    // F2 role: row `tid` of the R1 rows; B2 role: output row `tid` of the band.
-    const int hr2 = h0 - LAG + RAD + tid;               // image row of the F2 row
-    const bool row_in = hr2 >= 0 && hr2 < H;
-    const bool row_owned = row_in && (FUSED ? (tid >= RAD && tid < RAD + T) : true);
-    const int hg = h0 + tid;                            // image row of the B2 row
-    const bool grow_owned = FUSED && tid < T && hg < H;
-    const int64_t grow_base = ibase + static_cast<int64_t>(C) * (grow_owned ? hg : 0);
+    // F2 role: row `tid` of the band
+    const int hr2 = h0 + tid;                           // image row of the F2 row
+    const bool row_owned = hr2 < H;
 
     float2 hA[HIST], hB[HIST];          // (mx, my), (E[x^2+y^2], E[xy]) history of F1 columns
-    float2 gQM[HIST];                   // (2 dQ, dM) history of B1 columns
-    float gP[HIST];                     // dP history of B1 columns
 #pragma unroll
     for (int m = 0; m < HIST; ++m) {
         hA[m] = make_float2(0.f, 0.f);
         hB[m] = make_float2(0.f, 0.f);
-        gQM[m] = make_float2(0.f, 0.f);
-        gP[m] = 0.f;
     }
     double tsum = 0.0;
 
@@ -382,7 +331,7 @@ __global__ void __launch_bounds__(NT, (FUSED || !F32IO) ? 2 : 3) band_kernel(con
     for (int k = 0; k < ns; ++k) {
         // ---------------- F1: h-direction pass of the 4 moment images ----------------
         {
-            const float2* st = F32IO ? stage + (k & 1) * (R2 * SP) : stage;
+            const float2* st = stage + (k & 1) * (R2 * SP);
 #pragma unroll 1
             for (int it = 0; it < G::IT1; ++it) {
                 const int item = tid + NT * it;
@@ -414,15 +363,10 @@ __global__ void __launch_bounds__(NT, (FUSED || !F32IO) ? 2 : 3) band_kernel(con
         }
         __syncthreads();
 
-        // ---------------- F2: w-direction pass, SSIM map, partials ----------------
+        // ---------------- F2: w-direction pass and the SSIM map ----------------
         {
             // the staging buffer F1 just read is free: refill it two steps ahead
-            if (F32IO) {
-                issue_async(k + 2, stage + (k & 1) * (R2 * SP));
-            } else {
-                store_stage();       // step k+1, held in registers since the last step
-                issue_loads(k + 2);
-            }
+            issue_async(k + 2, stage + (k & 1) * (R2 * SP));
 
             const int wcb = w0 - LAG + k * S - RAD;   // image column of output o = 0
             float2 nA[S], nB[S];
@@ -451,130 +395,25 @@ __global__ void __launch_bounds__(NT, (FUSED || !F32IO) ? 2 : 3) band_kernel(con
                 const float t = (qs - sumsq) + p.C2;                 // vx + vy + C2
                 const float2 ab = __ffma2_rn(make_float2(2.f, 2.f), make_float2(mxy, pxy - mxy),
                                              make_float2(p.C1, p.C2));   // (2 mx my + C1, 2 cov + C2)
-                const float ax = ab.x, by = ab.y;
-                const float inv = rcp_approx(z * t);
-                const float s = (ax * by) * inv;
+                const float s = (ab.x * ab.y) * rcp_approx(z * t);
                 const int wc = wcb + o;                              // image column of this pixel
-                if (WANT_SSIM) {
-                    if (row_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc)) ssum += s;
-                }
-                if (FUSED) {
-                    // dS/dQ = -s/t, dS/dM = 2/(zt) ((by-ax) my + s (z-t) mx), dS/dP = 2 ax/(zt)
-                    // (src/core.jl:384-388; docs/src/math.md, "Gradients"), times +-1/N and
-                    // zero outside the image; dQ is stored doubled (it is used as 2x dQ).
-                    const bool in_img = row_in && static_cast<unsigned>(wc) < static_cast<unsigned>(W);
-                    const float inv2 = in_img ? 2.f * p.gscale * inv : 0.f;
-                    const float dq2 = -(s * z) * inv2;             // 2 dQ = -2 s/t = -2 s z / (zt)
-                    const float dm = inv2 * fmaf(by - ax, my, (s * (z - t)) * mx);
-                    const float dp = ax * inv2;
-                    qmp[tid * FC + o] = make_float4(dq2, dm, dp, 0.f);
-                }
+                if (row_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc)) ssum += s;
             }
-            if (WANT_SSIM) tsum += static_cast<double>(ssum);
+            tsum += static_cast<double>(ssum);
 #pragma unroll
             for (int m = 0; m < HIST; ++m) {
                 const int src = m + S;
                 hA[m] = (src < HIST) ? hA[src] : nA[src - HIST];
                 hB[m] = (src < HIST) ? hB[src] : nB[src - HIST];
             }
-            if (F32IO) cp_async_wait<1>();   // step k+1 has landed (k+2 may still fly)
+            cp_async_wait<1>();   // step k+1 has landed (k+2 may still fly)
         }
         __syncthreads();
-
-        if (FUSED) {
-            // ---------------- B1: h-direction pass of the partials ----------------
-#pragma unroll 1
-            for (int it = 0; it < G::ITB; ++it) {
-                const int item = tid + NT * it;
-                const int j1 = item % S, q1 = item / S;
-                if (q1 < NRUNB) {
-                    float2 aQM[V];
-                    float aP[V];
-#pragma unroll
-                    for (int o = 0; o < V; ++o) {
-                        aQM[o] = make_float2(0.f, 0.f);
-                        aP[o] = 0.f;
-                    }
-#pragma unroll
-                    for (int i = 0; i < V + 2 * RAD; ++i) {
-                        const float4 v = qmp[(V * q1 + i) * FC + j1];
-                        const float2 qm = make_float2(v.x, v.y);
-#pragma unroll
-                        for (int o = 0; o < V; ++o) {
-                            const int tap = i - o;
-                            if (tap >= 0 && tap < TAPS) {
-                                aQM[o] = __ffma2_rn(qm, FSSIM_K2(tap), aQM[o]);
-                                aP[o] = fmaf(v.z, FSSIM_K1(tap), aP[o]);
-                            }
-                        }
-                    }
-#pragma unroll
-                    for (int o = 0; o < V; ++o)
-                        b1buf[(V * q1 + o) * FC + j1] = make_float4(aQM[o].x, aQM[o].y, aP[o], 0.f);
-                }
-            }
-            __syncthreads();
-
-            // ---------------- B2: w-direction pass and the combine ----------------
-            {
-                const int wcg = w0 - LAG + k * S - 2 * RAD;   // image column of output o = 0
-                float2 nQM[S];
-                float nP[S];
-#pragma unroll
-                for (int o = 0; o < S; ++o) {
-                    {
-                        const float4 v = b1buf[tid * FC + o];
-                        nQM[o] = make_float2(v.x, v.y);
-                        nP[o] = v.z;
-                    }
-                    float2 a = make_float2(0.f, 0.f);
-                    float bp = 0.f;
-#pragma unroll
-                    for (int tap = 0; tap < TAPS; ++tap) {
-                        const int m = o + tap;
-                        const float2 wq = (m < HIST) ? gQM[m] : nQM[m - HIST];
-                        const float wp = (m < HIST) ? gP[m] : nP[m - HIST];
-                        a = __ffma2_rn(wq, FSSIM_K2(tap), a);
-                        bp = fmaf(wp, FSSIM_K1(tap), bp);
-                    }
-                    const int wc = wcg + o;
-                    const bool own = grow_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc);
-                    // loads are unconditional (a valid address when not owned); only the store is predicated
-                    const int64_t g = grow_base + CH * (own ? wc : 0);
-                    float xv, yv;
-                    if (F32IO) {
-                        xv = __ldg(reinterpret_cast<const float*>(p.x) + g);
-                        yv = __ldg(reinterpret_cast<const float*>(p.y) + g);
-                    } else {
-                        xv = cvt_raw(ld_raw(p.x, p.xdt, g), p.xdt, nullptr);
-                        yv = cvt_raw(ld_raw(p.y, p.ydt, g), p.ydt, nullptr);
-                    }
-                    // src/core.jl:773-782: (2 x K(dQ) + K(dM) + y K(dP)) * N_inv (N_inv folded upstream)
-                    const float gv = fmaf(yv, bp, fmaf(xv, a.x, a.y));
-                    if (own) {
-                        if (F32IO) reinterpret_cast<float*>(p.grad)[g] = gv;
-                        else st_grad(p.grad, p.gdt, g, gv);
-                    }
-                }
-#pragma unroll
-                for (int m = 0; m < HIST; ++m) {
-                    const int src = m + S;
-                    gQM[m] = (src < HIST) ? gQM[src] : nQM[src - HIST];
-                    gP[m] = (src < HIST) ? gP[src] : nP[src - HIST];
-                }
-            }
-            // No barrier here: the next step writes f1buf (last read before the F2
-            // barrier), the staging buffer (read before the F1 barrier), qmp (read
-            // before the B1 barrier) and b1buf only after two more barriers.
-        }
     }
 #undef FSSIM_K2
-#undef FSSIM_K1
 
-    if (WANT_SSIM) {
-        const int local_cta = (band * p.nseg + seg) * p.C + c;
-        finish_image<NT>(p, n, local_cta, tsum, red);
-    }
+    const int local_cta = (band * p.nseg + seg) * p.C + c;
+    finish_image<NT>(p, n, local_cta, tsum, red);
 }
 
 }  // namespace fssim
@@ -1015,6 +854,199 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
         const int local_cta = (band * p.nseg + seg) * p.C + c;
         finish_image<2 * NT>(p, n, local_cta, tsum, red);
     }
+}
+
+}  // namespace fssim
+
+namespace fssim {
+
+// ---------------------------------------------------------------------------
+// Tile kernel for small forward-only calls (a single image, a few images).
+//
+// The streaming kernels cut a lone full-HD image into many short segments, each
+// of which streams 10 halo columns and waits on two barriers per step, with two
+// warps per CTA.  Here a CTA of 256 threads computes the SSIM map of one
+// TH x TW output tile of one channel in three phases, with the whole input
+// tile loaded at once:
+//   load  (TH+10) x (TW+10) inputs of x and y (converted to Float32) -> stage
+//   F1    h-direction 11-tap pass of the 4 moment images, all TW+10 columns
+//   F2    w-direction pass, SSIM map and the tile's sum
+// Shared-memory strides are odd (in 8- and 16-byte units), so the column reads
+// of F1 and the row reads of F2 are conflict-free.
+// ---------------------------------------------------------------------------
+struct TGeo {
+    static constexpr int TH = 32, TW = 54;           // output tile: rows (h) x columns (w)
+    static constexpr int NT = 256;
+    static constexpr int IR = TH + 2 * RAD;          // input rows
+    static constexpr int IC = TW + 2 * RAD;          // input columns = F1 output columns
+    static constexpr int RS = IR + 1;                // stage column stride (float2), odd
+    static constexpr int NG = (TW + V - 1) / V;      // F2 column groups of V outputs per row
+    static constexpr int FS = NG * V + 2 * RAD + 1;  // F1 row stride (float4), odd, covers the last group
+    static constexpr int NE = IR * IC;               // staged elements
+    static constexpr int NL = (NE + NT - 1) / NT;    // staged elements per thread
+    static constexpr int stage_one = IC * RS * 8;
+    static constexpr int f1_bytes = TH * FS * 16;
+    static constexpr int red_bytes = (NT / 32 + 2) * 8;
+    static constexpr int total = stage_one + f1_bytes + red_bytes;
+    static_assert(IC * (TH / V) == NT, "one F1 item per thread");
+    static_assert(TH * NG <= NT, "one F2 item per thread");
+    static_assert(RS % 2 == 1 && FS % 2 == 1, "odd strides");
+    static_assert(stage_one % 16 == 0, "f1 stays 16-byte aligned");
+};
+
+// IM: 0 = Float32 inputs, otherwise an InMode (N0f8 / Float16 / any, converted).
+// CTA t computes tile t; the loop over t (stride gridDim.x) also serves grids
+// smaller than the tile count.  A resident CTA's next tile streaming in behind
+// the current one was measured slower: it halves the CTAs per SM.
+template <int IM>
+__global__ void __launch_bounds__(TGeo::NT, 3) tile_fwd_kernel(const Params p)
+{
+    using G = TGeo;
+    constexpr int TH = G::TH, TW = G::TW, IR = G::IR, IC = G::IC, RS = G::RS, FS = G::FS;
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float2* stage = reinterpret_cast<float2*>(smem_raw);                  // [IC][RS], (x, y)
+    float4* f1 = reinterpret_cast<float4*>(smem_raw + G::stage_one);      // [TH][FS]
+    double* red = reinterpret_cast<double*>(smem_raw + G::stage_one + G::f1_bytes);
+
+    const int tid = threadIdx.x;
+    const int C = p.C, H = p.H, W = p.W;
+    const int64_t CH = static_cast<int64_t>(C) * H;
+    const int64_t ntiles = static_cast<int64_t>(p.N) * p.cpi;
+    struct Tile {
+        int n, th, tw, c;
+        int64_t ibase;
+    };
+    auto tile_of = [&](int64_t t) {
+        Tile u;
+        u.c = static_cast<int>(t % C);
+        t /= C;
+        u.tw = static_cast<int>(t % p.nseg);
+        t /= p.nseg;
+        u.th = static_cast<int>(t % p.nb);
+        u.n = static_cast<int>(t / p.nb);
+        u.ibase = static_cast<int64_t>(u.n) * p.img_elems + u.c;
+        return u;
+    };
+    // element e of a tile <-> stage row r = e % IR, column q = e / IR; zero outside the image;
+    // all loads of the tile are issued before the first conversion
+    auto load_convert = [&](int64_t t, float2* buf) {
+        const Tile u = tile_of(t);
+        uint32_t rx[G::NL], ry[G::NL];
+#pragma unroll
+        for (int k = 0; k < G::NL; ++k) {
+            const int e = tid + G::NT * k;
+            const int r = e % IR, q = e / IR;
+            const int hr = u.th * TH - RAD + r, wc = u.tw * TW - RAD + q;
+            const bool ok = e < G::NE && hr >= 0 && hr < H && wc >= 0 && wc < W;
+            const int64_t g = u.ibase + static_cast<int64_t>(C) * (ok ? hr : 0) + CH * (ok ? wc : 0);
+            if (IM == 0) {
+                rx[k] = ok ? __ldg(reinterpret_cast<const unsigned int*>(p.x) + g) : 0u;
+                ry[k] = ok ? __ldg(reinterpret_cast<const unsigned int*>(p.y) + g) : 0u;
+            } else {
+                rx[k] = ok ? ld_in<IM>(p.x, p.xdt, g) : 0u;
+                ry[k] = ok ? ld_in<IM>(p.y, p.ydt, g) : 0u;
+            }
+        }
+#pragma unroll
+        for (int k = 0; k < G::NL; ++k) {
+            const int e = tid + G::NT * k;
+            if (e < G::NE)
+                buf[(e / IR) * RS + e % IR] =
+                    IM == 0 ? make_float2(__uint_as_float(rx[k]), __uint_as_float(ry[k]))
+                            : make_float2(cvt_in<IM>(rx[k], p.xdt), cvt_in<IM>(ry[k], p.ydt));
+        }
+    };
+
+    // F1 columns past IC feed only outputs outside the tile: keep them finite
+    for (int e = tid; e < TH * (FS - IC); e += G::NT)
+        f1[(e / (FS - IC)) * FS + IC + e % (FS - IC)] = make_float4(0.f, 0.f, 0.f, 0.f);
+    float2 KP[RAD + 1];
+#pragma unroll
+    for (int i = 0; i <= RAD; ++i) KP[i] = make_float2(p.kh[i], p.kh[i]);
+#define FSSIM_K2(tap) KP[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
+
+#pragma unroll 1
+    for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
+        float2* st = stage;
+        load_convert(t, st);
+        __syncthreads();   // the stage is complete; the previous tile's F2 is done with f1
+        const Tile u = tile_of(t);
+
+        // ---- F1: rows V*q1 .. V*q1+V-1 of column q (stage rows V*q1 .. V*q1+V+2R-1)
+        {
+            const int q = tid % IC, q1 = tid / IC;
+            float2 aA[V], aB[V];
+#pragma unroll
+            for (int o = 0; o < V; ++o) {
+                aA[o] = make_float2(0.f, 0.f);
+                aB[o] = make_float2(0.f, 0.f);
+            }
+#pragma unroll
+            for (int i = 0; i < V + 2 * RAD; ++i) {
+                const float2 xy = st[q * RS + V * q1 + i];
+                const float2 sq = __fmul2_rn(xy, xy);
+                const float2 sb = make_float2(sq.x + sq.y, xy.x * xy.y);     // (x^2+y^2, xy)
+#pragma unroll
+                for (int o = 0; o < V; ++o) {
+                    const int tap = i - o;
+                    if (tap >= 0 && tap < TAPS) {
+                        aA[o] = __ffma2_rn(xy, FSSIM_K2(tap), aA[o]);
+                        aB[o] = __ffma2_rn(sb, FSSIM_K2(tap), aB[o]);
+                    }
+                }
+            }
+#pragma unroll
+            for (int o = 0; o < V; ++o)
+                f1[(V * q1 + o) * FS + q] = make_float4(aA[o].x, aA[o].y, aB[o].x, aB[o].y);
+        }
+        __syncthreads();
+
+        // ---- F2 + map: row r, output columns V*g .. V*g+V-1 of the tile
+        double tsum = 0.0;
+        {
+            const int r = tid % TH, g = tid / TH;
+            if (g < G::NG) {
+                float2 a[V], b[V];
+#pragma unroll
+                for (int o = 0; o < V; ++o) {
+                    a[o] = make_float2(0.f, 0.f);
+                    b[o] = make_float2(0.f, 0.f);
+                }
+#pragma unroll
+                for (int m = 0; m < V + 2 * RAD; ++m) {
+                    const float4 v = f1[r * FS + V * g + m];
+                    const float2 va = make_float2(v.x, v.y), vb = make_float2(v.z, v.w);
+#pragma unroll
+                    for (int o = 0; o < V; ++o) {
+                        const int tap = m - o;
+                        if (tap >= 0 && tap < TAPS) {
+                            a[o] = __ffma2_rn(va, FSSIM_K2(tap), a[o]);
+                            b[o] = __ffma2_rn(vb, FSSIM_K2(tap), b[o]);
+                        }
+                    }
+                }
+                const int hr = u.th * TH + r, w0 = u.tw * TW;
+                float ssum = 0.f;
+#pragma unroll
+                for (int o = 0; o < V; ++o) {
+                    const float mx = a[o].x, my = a[o].y, qs = b[o].x, pxy = b[o].y;
+                    const float2 sq = __fmul2_rn(a[o], a[o]);
+                    const float mxy = mx * my;
+                    const float sumsq = sq.x + sq.y;
+                    const float z = sumsq + p.C1;
+                    const float tt = (qs - sumsq) + p.C2;
+                    const float ax = fmaf(2.f, mxy, p.C1);
+                    const float by = fmaf(2.f, pxy - mxy, p.C2);
+                    const float sv = (ax * by) * rcp_approx(z * tt);
+                    const int col = V * g + o;
+                    if (hr < H && col < TW && w0 + col < W) ssum += sv;
+                }
+                tsum = static_cast<double>(ssum);
+            }
+        }
+        finish_image<G::NT>(p, u.n, (u.th * p.nseg + u.tw) * C + u.c, tsum, red);
+    }
+#undef FSSIM_K2
 }
 
 }  // namespace fssim
