@@ -211,3 +211,28 @@ def test_float64_gradient_output_from_float32_inputs(pkg, orc):
     pkg.ssim_gradient_(g, xt, yt, None)
     _, rg = orc.ssim(x, y, precision="f32")
     assert _rel_l2(pkg.jl_to_numpy(g), rg) <= GRAD_RTOL_L2
+
+
+@pytest.mark.parametrize("shape", [(3, 1100, 1400, 1), (1, 600, 800, 10)], ids=["3x1100x1400", "10x1x600x800"])
+def test_forward_streaming_kernel_vs_oracle(pkg, orc, shape):
+    """Float32 forward calls above 4 Mi elements take the streaming kernel (smaller ones and
+    converted inputs run as tiles): the same tolerance against the float64 oracle."""
+    x, y = _syn(pkg).host_pair(29, shape, 0.1)
+    v, _ = _run(pkg, x, y, mode="fwd")
+    rv, _ = orc.ssim(x, y, flags=orc.SKIP_BACKWARD, precision="f64")
+    assert np.max(np.abs(v - rv)) <= SSIM_ATOL, (v, rv)
+    v, _ = _run(pkg, x, y, mode="fwd", dssim=True, div2=True)
+    assert np.max(np.abs(v - (1.0 - rv) / 2)) <= SSIM_ATOL
+
+
+def test_forward_tile_and_streaming_kernels_agree_across_the_threshold(pkg):
+    """A batch just above the tile threshold (streaming) and its images computed one at a
+    time (tiles) give the same per-image values within the tolerance."""
+    x, y = _syn(pkg).host_pair(31, (3, 700, 700, 3), 0.1)        # 4.41 Mi elements: streaming
+    xt, yt = pkg.jl_from_numpy(x), pkg.jl_from_numpy(y)
+    whole = torch.empty(3, dtype=torch.float32, device="cuda")
+    pkg.ssim_(whole, xt, yt)
+    single = torch.empty(1, dtype=torch.float32, device="cuda")
+    for i in range(3):                                               # 1.47 Mi elements each: tiles
+        pkg.ssim_(single, xt[..., i:i + 1], yt[..., i:i + 1])
+        assert abs(float(single[0]) - float(whole[i])) <= SSIM_ATOL
