@@ -25,6 +25,22 @@ _ws_lock = threading.Lock()
 _workspaces: dict[tuple[int, int], torch.Tensor] = {}
 
 
+# fssim_workspace_size results per (sizes, flags, device): the value depends only
+# on those, and computing it configures every kernel variant.
+_ws_sizes: dict[tuple[int, int, int, int, int, int], int] = {}
+
+
+def _workspace_size(c: int, h: int, w: int, n: int, flags: int, device_index: int) -> int:
+    key = (c, h, w, n, flags, device_index)
+    nbytes = _ws_sizes.get(key)
+    if nbytes is None:
+        nbytes = nat.workspace_size(c, h, w, n, flags)
+        if len(_ws_sizes) > 4096:
+            _ws_sizes.clear()
+        _ws_sizes[key] = nbytes
+    return nbytes
+
+
 def _workspace(device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> torch.Tensor | None:
     if nbytes == 0:
         return None
@@ -142,9 +158,14 @@ def ssim_fwd_bwd(ssims, dL_dimgs1, imgs1, imgs2, N_dssims_dQMP, should_zero: boo
             if t.device != device:
                 raise ValueError(f"{name} is on {t.device}, expected {device}")
 
-    with torch.cuda.device(device):
+    # the library launches on the current device: switch only when it differs
+    switch = device.index != torch.cuda.current_device()
+    prev = torch.cuda.current_device() if switch else None
+    if switch:
+        torch.cuda.set_device(device)
+    try:
         stream = torch.cuda.current_stream(device)
-        nbytes = nat.workspace_size(c, h, w, b, flags)
+        nbytes = _workspace_size(c, h, w, b, flags, device.index)
         ws = _workspace(device, stream, nbytes)
         out_args = (ssims.data_ptr() if not skip_ssim else 0, dtype_code(ssims) if not skip_ssim else nat.FLOAT32,
                     b if skip_ssim else int(ssims.shape[0]),
@@ -158,6 +179,9 @@ def ssim_fwd_bwd(ssims, dL_dimgs1, imgs1, imgs2, N_dssims_dQMP, should_zero: boo
         else:
             nat.fwd_bwd_scaled(*out_args, c, h, w, b, flags, grad_scale.data_ptr(), dtype_code(grad_scale),
                                *ws_args)
+    finally:
+        if switch:
+            torch.cuda.set_device(prev)
 
     if not skip_ssim and allocated_ssims and should_unpack(ssims, imgs1):
         ssims = ssims.item()           # the reference's blocking scalar read
