@@ -240,9 +240,10 @@ __device__ __forceinline__ void finish_image(const Params& p, int n, int local_c
 
 // Forward-only streaming kernel for Float32 inputs (SSIM values, no gradient).
 // Loads go straight to shared memory with cp.async, double-buffered two steps
-// ahead; two barriers per step (after F1, after F2).
+// ahead; two barriers per step (after F1, after F2).  The launch bound keeps
+// 16 warps per SM resident (at most 128 registers a thread, no spills).
 template <int NT>
-__global__ void __launch_bounds__(NT, 3) band_kernel(const Params p)
+__global__ void __launch_bounds__(NT, 512 / NT) band_kernel(const Params p)
 {
     using G = Geo<NT>;
     constexpr int S = G::S, T = G::T, R2 = G::R2, LAG = G::LAG;
