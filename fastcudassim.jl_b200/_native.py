@@ -30,7 +30,7 @@ ERR_MISALIGNED = 5
 ERR_CUDA = 6
 
 EXPORTED_SYMBOLS = ("fssim_version", "fssim_last_error", "fssim_workspace_size", "fssim_fwd_bwd",
-                    "fssim_fwd_bwd_scaled", "fssim_fwd_bwd_noalloc")
+                    "fssim_fwd_bwd_scaled", "fssim_fwd_bwd_noalloc", "fssim_debug_bounds_status")
 # Size of the scratch array behind fssim_fwd_bwd_noalloc (FSSIM_NOALLOC_SCRATCH_BYTES).
 NOALLOC_SCRATCH_BYTES = 4 << 20
 
@@ -75,6 +75,9 @@ def load() -> ctypes.CDLL:
     lib.fssim_fwd_bwd_noalloc.argtypes = [vp, ctypes.c_int, i64, vp, ctypes.c_int, vp, ctypes.c_int, vp,
                                           ctypes.c_int, i64, i64, i64, i64, u32, vp]
     lib.fssim_fwd_bwd_noalloc.restype = ctypes.c_int
+    lib.fssim_debug_bounds_status.argtypes = [ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_ulonglong),
+                                              ctypes.c_int]
+    lib.fssim_debug_bounds_status.restype = ctypes.c_int
     _lib = lib
     return lib
 
@@ -133,3 +136,10 @@ def fwd_bwd_noalloc(ssims_ptr: int, ssims_dtype: int, ssims_len: int, grad_ptr: 
     check(load().fssim_fwd_bwd_noalloc(ssims_ptr or None, ssims_dtype, ssims_len, grad_ptr or None, grad_dtype,
                                        x_ptr or None, x_dtype, y_ptr or None, y_dtype, c, h, w, n, flags,
                                        stream or None))
+
+
+def debug_bounds_status(reset: bool = True) -> tuple[int, int]:
+    """``fssim_debug_bounds_status`` of a bounds-checked build: (first failing site, count)."""
+    site, count = ctypes.c_uint(0), ctypes.c_ulonglong(0)
+    check(load().fssim_debug_bounds_status(ctypes.byref(site), ctypes.byref(count), int(reset)))
+    return int(site.value), int(count.value)

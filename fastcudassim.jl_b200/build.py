@@ -15,6 +15,8 @@ ROOT = os.path.dirname(HERE)
 SRC = [os.path.join(HERE, "csrc", "fssim.cu")]
 DEPS = SRC + [os.path.join(HERE, "csrc", "fssim_kernels.cuh"), os.path.join(ROOT, "include", "fastssim.h")]
 OUT = os.path.join(HERE, "lib", "libfastssim.so")
+# The same sources with every global access bounds-checked (tests only).
+OUT_BOUNDS = os.path.join(HERE, "lib", "libfastssim_bounds.so")
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
               "-Xcompiler", "-fPIC", "-shared", "-cudart", "static"]
@@ -27,20 +29,28 @@ def nvcc() -> str:
     return "nvcc"
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    os.makedirs(os.path.dirname(OUT), exist_ok=True)
-    if not force and os.path.exists(OUT):
+def build(force: bool = False, verbose: bool = False, bounds: bool = False) -> str:
+    """Build the library (or, with ``bounds``, its bounds-checked variant) unless it
+    is newer than every source."""
+    out = OUT_BOUNDS if bounds else OUT
+    os.makedirs(os.path.dirname(out), exist_ok=True)
+    if not force and os.path.exists(out):
         newest = max(os.path.getmtime(p) for p in DEPS)
-        if os.path.getmtime(OUT) >= newest:
-            return OUT
+        if os.path.getmtime(out) >= newest:
+            return out
     cmd = [nvcc(), *NVCC_FLAGS, "-I", os.path.join(ROOT, "include"), "-I", os.path.join(HERE, "csrc"),
-           "-o", OUT, *SRC]
+           "-o", out, *SRC]
+    if bounds:
+        cmd.insert(1, "-DFSSIM_DEBUG_BOUNDS")
     if verbose:
         cmd.insert(1, "-Xptxas=-v")
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)
-    return OUT
+    return out
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    force, verbose = "--force" in sys.argv, "-v" in sys.argv
+    print(build(force=force, verbose=verbose))
+    if "--bounds" in sys.argv:
+        print(build(force=force, verbose=verbose, bounds=True))

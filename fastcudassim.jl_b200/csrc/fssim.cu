@@ -312,7 +312,34 @@ int check_sizes(int64_t c, int64_t h, int64_t w, int64_t n)
 
 extern "C" {
 
+#ifdef FSSIM_DEBUG_BOUNDS
+const char* fssim_version(void) { return "fastssim 0.1.0 (abi 1, sm_100a, bounds-checked)"; }
+#else
 const char* fssim_version(void) { return "fastssim 0.1.0 (abi 1, sm_100a)"; }
+#endif
+
+int fssim_debug_bounds_status(unsigned* first_site, unsigned long long* count, int reset)
+{
+#ifdef FSSIM_DEBUG_BOUNDS
+    if (!first_site || !count) return fail(FSSIM_ERR_INVALID_ARGUMENT, "first_site and count must not be NULL");
+    cudaError_t e = cudaDeviceSynchronize();
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(first_site, fssim::g_fssim_bounds_site, sizeof(unsigned));
+    if (e == cudaSuccess) e = cudaMemcpyFromSymbol(count, fssim::g_fssim_bounds_count, sizeof(unsigned long long));
+    if (e == cudaSuccess && reset) {
+        const unsigned z = 0u;
+        const unsigned long long zz = 0ull;
+        e = cudaMemcpyToSymbol(fssim::g_fssim_bounds_site, &z, sizeof(z));
+        if (e == cudaSuccess) e = cudaMemcpyToSymbol(fssim::g_fssim_bounds_count, &zz, sizeof(zz));
+    }
+    if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "bounds status: %s", cudaGetErrorString(e));
+    return ok();
+#else
+    (void)first_site;
+    (void)count;
+    (void)reset;
+    return fail(FSSIM_ERR_INVALID_ARGUMENT, "this library was built without FSSIM_DEBUG_BOUNDS");
+#endif
+}
 
 int fssim_last_error(char* buf, size_t len)
 {
@@ -416,6 +443,7 @@ int fwd_bwd_impl(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs
     p.counters = want_ssim ? static_cast<unsigned*>(workspace) : nullptr;
     p.partials = want_ssim ? reinterpret_cast<double*>(static_cast<char*>(workspace) + g.ws_counters) : nullptr;
     p.img_elems = c * h * w;
+    p.total_elems = c * h * w * n;
     p.C = static_cast<int>(c);
     p.H = static_cast<int>(h);
     p.W = static_cast<int>(w);

@@ -62,6 +62,7 @@ struct Params {
     double* partials;         // workspace: N * cpi doubles
     unsigned int* counters;   // workspace: N counters, zero between calls
     int64_t img_elems;        // C*H*W
+    int64_t total_elems;      // N*C*H*W (bounds of x, y and the gradient)
     int C, H, W, N;
     int nb, nseg, L;          // bands, segments, segment length (columns)
     int cpi;                  // CTAs per image = C * nb * nseg
@@ -81,6 +82,30 @@ __device__ __forceinline__ float rcp_approx(float v)
     asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(v));
     return r;
 }
+
+// Opt-in bounds checking (built with -DFSSIM_DEBUG_BOUNDS, the library's stand-in
+// for a memory checker): every global access first checks its element index
+// against the array it addresses.  An index out of range is recorded (the first
+// failing site and a count) and the access is skipped instead of made.
+#ifdef FSSIM_DEBUG_BOUNDS
+__device__ unsigned g_fssim_bounds_site;
+__device__ unsigned long long g_fssim_bounds_count;
+__device__ __forceinline__ bool in_bounds(int64_t idx, int64_t limit, unsigned site)
+{
+    if (idx >= 0 && idx < limit) return true;
+    atomicCAS(&g_fssim_bounds_site, 0u, site);
+    atomicAdd(&g_fssim_bounds_count, 1ull);
+    return false;
+}
+#define FSSIM_IN_BOUNDS(idx, limit, site) ::fssim::in_bounds((idx), (limit), (site))
+#else
+#define FSSIM_IN_BOUNDS(idx, limit, site) true
+#endif
+// Site numbers reported by the bounds-checked build.
+enum BoundsSite : unsigned {
+    SITE_BAND_LOAD = 1, SITE_PIPE_STAGE, SITE_PIPE_XY, SITE_PIPE_STAGE_RAW, SITE_PIPE_XY_RAW,
+    SITE_PIPE_GRAD, SITE_TILE_LOAD, SITE_F64_LOAD, SITE_F64_GRAD, SITE_PARTIALS, SITE_COUNTERS
+};
 
 // Raw bits of one input element (zero-extended); converted at staging time so
 // that the load's latency is not exposed at the point of issue.
@@ -215,10 +240,16 @@ __device__ __forceinline__ void finish_image(const Params& p, int n, int local_c
 {
     const double tot = block_sum<NT>(tsum, red);
     if (threadIdx.x == 0) {
-        p.partials[(int64_t)n * p.cpi + local_cta] = tot;
-        __threadfence();
-        const unsigned prev = atomicAdd(&p.counters[n], 1u);
-        red[NT / 32] = (prev == static_cast<unsigned>(p.cpi - 1)) ? 1.0 : 0.0;
+        const int64_t slot = (int64_t)n * p.cpi + local_cta;
+        const bool ok = FSSIM_IN_BOUNDS(slot, (int64_t)p.N * p.cpi, SITE_PARTIALS) &&
+                        FSSIM_IN_BOUNDS(n, p.N, SITE_COUNTERS);
+        unsigned prev = 0u;
+        if (ok) {
+            p.partials[slot] = tot;
+            __threadfence();
+            prev = atomicAdd(&p.counters[n], 1u);
+        }
+        red[NT / 32] = (ok && prev == static_cast<unsigned>(p.cpi - 1)) ? 1.0 : 0.0;
     }
     __syncthreads();
     if (red[NT / 32] != 0.0) {   // uniform over the CTA; no early return, so loops may call this
@@ -300,7 +331,8 @@ __global__ void __launch_bounds__(NT, 512 / NT) band_kernel(const Params p)
 #pragma unroll
                 for (int j = 0; j < S; ++j) {
                     const int wc = cb + j;
-                    const bool ok = lrow_ok[r] && k < ns && static_cast<unsigned>(wc) < static_cast<unsigned>(W);
+                    bool ok = lrow_ok[r] && k < ns && static_cast<unsigned>(wc) < static_cast<unsigned>(W);
+                    ok = ok && FSSIM_IN_BOUNDS(lrow_base[r] + CH * wc, p.total_elems, SITE_BAND_LOAD);
                     const int64_t g = ok ? lrow_base[r] + CH * wc : 0;
                     float2* d = buf + i * SP + j;
                     cp_async4(&d->x, reinterpret_cast<const float*>(p.x) + g, ok);
@@ -561,8 +593,9 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
                 for (int r = 0; r < G::LROWS; ++r) {
                     const int i = ta + NT * r;
                     if (G::LROWS == 1 || i < R2) {
-                        const bool ok = lrow_ok[r] && colok;
                         const uint32_t off = lrow_off[r] + coloff;
+                        const bool ok = lrow_ok[r] && colok &&
+                                        FSSIM_IN_BOUNDS(ibase + off, p.total_elems, SITE_PIPE_STAGE);
                         cp_async4(&buf[i * SP + j].x, xg + off, ok);
                         cp_async4(&buf[i * SP + j].y, yg + off, ok);
                     }
@@ -574,8 +607,9 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
 #pragma unroll
             for (int o = 0; o < S; ++o) {
                 const int wc = cb + o;
-                const bool ok = xyrow_ok && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc);
+                bool ok = xyrow_ok && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc);
                 const uint32_t off = xyrow_off + CH32 * static_cast<uint32_t>(ok ? wc : 0);
+                ok = ok && FSSIM_IN_BOUNDS(ibase + off, p.total_elems, SITE_PIPE_XY);
                 cp_async4(&buf[ta * SP + o].x, xg + off, ok);
                 cp_async4(&buf[ta * SP + o].y, yg + off, ok);
             }
@@ -593,8 +627,8 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
                 const bool colok = static_cast<unsigned>(wc) < static_cast<unsigned>(W);
 #pragma unroll
                 for (int r = 0; r < G::LROWS; ++r) {
-                    const bool ok = lrow_ok[r] && colok;
                     const int64_t g = ibase + (lrow_off[r] + CH32 * static_cast<uint32_t>(colok ? wc : 0));
+                    const bool ok = lrow_ok[r] && colok && FSSIM_IN_BOUNDS(g, p.total_elems, SITE_PIPE_STAGE_RAW);
                     rsx[r * S + j] = ok ? ld_in<IOM>(p.x, p.xdt, g) : 0u;
                     rsy[r * S + j] = ok ? ld_in<IOM>(p.y, p.ydt, g) : 0u;
                 }
@@ -617,8 +651,9 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
 #pragma unroll
             for (int o = 0; o < (F32IO ? 0 : S); ++o) {
                 const int wc = cb + o;
-                const bool ok = xyrow_ok && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc);
+                bool ok = xyrow_ok && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc);
                 const int64_t g = ibase + (xyrow_off + CH32 * static_cast<uint32_t>(ok ? wc : 0));
+                ok = ok && FSSIM_IN_BOUNDS(g, p.total_elems, SITE_PIPE_XY_RAW);
                 rxx[o] = ok ? ld_in<IOM>(p.x, p.xdt, g) : 0u;
                 rxy[o] = ok ? ld_in<IOM>(p.y, p.ydt, g) : 0u;
             }
@@ -827,8 +862,10 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
                     const float gv = fmaf(v.y, bp, fmaf(v.x, a.x, a.y));
                     if (grow_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc)) {
                         const uint32_t off = grow_off + CH32 * static_cast<uint32_t>(wc);
-                        if (IOM != IN_ANY) gg[off] = gv;
-                        else st_grad(p.grad, p.gdt, ibase + off, gv);
+                        if (FSSIM_IN_BOUNDS(ibase + off, p.total_elems, SITE_PIPE_GRAD)) {
+                            if (IOM != IN_ANY) gg[off] = gv;
+                            else st_grad(p.grad, p.gdt, ibase + off, gv);
+                        }
                     }
                 }
 #undef FSSIM_WQ
@@ -938,8 +975,9 @@ __global__ void __launch_bounds__(TGeo::NT, 3) tile_fwd_kernel(const Params p)
             const int e = tid + G::NT * k;
             const int r = e % IR, q = e / IR;
             const int hr = u.th * TH - RAD + r, wc = u.tw * TW - RAD + q;
-            const bool ok = e < G::NE && hr >= 0 && hr < H && wc >= 0 && wc < W;
+            bool ok = e < G::NE && hr >= 0 && hr < H && wc >= 0 && wc < W;
             const int64_t g = u.ibase + static_cast<int64_t>(C) * (ok ? hr : 0) + CH * (ok ? wc : 0);
+            ok = ok && FSSIM_IN_BOUNDS(g, p.total_elems, SITE_TILE_LOAD);
             if (IM == 0) {
                 rx[k] = ok ? __ldg(reinterpret_cast<const unsigned int*>(p.x) + g) : 0u;
                 ry[k] = ok ? __ldg(reinterpret_cast<const unsigned int*>(p.y) + g) : 0u;
@@ -1122,8 +1160,10 @@ __global__ void __launch_bounds__(D64Geo::NT) f64_kernel(const Params p)
         double xv = 0.0, yv = 0.0;
         if (hr >= 0 && hr < H && wc >= 0 && wc < W) {
             const int64_t g = ibase + static_cast<int64_t>(C) * hr + CH * wc;
-            xv = ld_f64(p.x, p.xdt, g);
-            yv = ld_f64(p.y, p.ydt, g);
+            if (FSSIM_IN_BOUNDS(g, p.total_elems, SITE_F64_LOAD)) {
+                xv = ld_f64(p.x, p.xdt, g);
+                yv = ld_f64(p.y, p.ydt, g);
+            }
         }
         xs[r * TI + q] = xv;
         ys[r * TI + q] = yv;
@@ -1211,6 +1251,7 @@ __global__ void __launch_bounds__(D64Geo::NT) f64_kernel(const Params p)
             const double xv = xs[(r + 2 * RAD) * TI + q + 2 * RAD], yv = ys[(r + 2 * RAD) * TI + q + 2 * RAD];
             const double gv = xv * cv[0] + cv[1] + yv * cv[2];     // 2 dQ is stored doubled
             const int64_t g = ibase + static_cast<int64_t>(C) * hg + CH * wg;
+            if (!FSSIM_IN_BOUNDS(g, p.total_elems, SITE_F64_GRAD)) continue;
             if (p.gdt == DT_F64) reinterpret_cast<double*>(p.grad)[g] = gv;
             else st_grad(p.grad, p.gdt, g, static_cast<float>(gv));
         }

@@ -71,6 +71,15 @@ typedef enum fssim_status {
 /* Library version string, e.g. "fastssim 0.1.0 (abi 1, sm_100a)". */
 const char* fssim_version(void);
 
+/* Bounds-checked builds only (compiled with -DFSSIM_DEBUG_BOUNDS: libfastssim_bounds.so).
+ * There every global-memory access checks its element index first; an index
+ * out of range is skipped and recorded.  Synchronises the current device, then
+ * reports the site number of the first failing access (0 = none) and the count
+ * of failing accesses since the last reset, and clears both if `reset`.  The
+ * regular build returns FSSIM_ERR_INVALID_ARGUMENT.  No counterpart in the
+ * reference (its kernels run under @inbounds, src/core.jl:186-187). */
+int fssim_debug_bounds_status(unsigned* first_site, unsigned long long* count, int reset);
+
 /* Copies the last error message of the calling thread into buf (NUL-terminated,
  * truncated to len).  Returns the status code of that error (FSSIM_OK if none). */
 int fssim_last_error(char* buf, size_t len);

@@ -79,3 +79,11 @@ def test_scaled_entry_point_argument_errors(pkg):
     st = lib.fssim_fwd_bwd_scaled(None, 0, 1, x, 0, x, 0, x, 0, 0, 8, 8, 1, nat.SKIP_SSIM, x, nat.FLOAT32,
                                   None, 0, None)
     assert st == nat.ERR_INVALID_ARGUMENT
+
+
+def test_bounds_status_needs_the_checked_build(pkg):
+    lib = pkg._native.load()
+    site, count = ctypes.c_uint(7), ctypes.c_ulonglong(7)
+    st = lib.fssim_debug_bounds_status(ctypes.byref(site), ctypes.byref(count), 0)
+    assert st == pkg._native.ERR_INVALID_ARGUMENT
+    assert "FSSIM_DEBUG_BOUNDS" in pkg._native.last_error()[1]
