@@ -454,10 +454,12 @@ __global__ void __launch_bounds__(NT, 512 / NT) band_kernel(const Params p)
 namespace fssim {
 
 // ---------------------------------------------------------------------------
-// Two-group pipelined kernel: SSIM + gradient, Float32 inputs and gradient.
+// Two-group pipelined kernel: SSIM + gradient (and gradient only), every input
+// and gradient dtype but Float64.
 //
-// The same streaming decomposition as band_kernel, but the CTA is split into
-// two warp groups of NT threads that work on different steps at once:
+// The streaming decomposition described at the top of this file, with the 5-row
+// gradient halo (T = NT - 10); the CTA is split into two warp groups of NT
+// threads that work on different steps at once:
 //
 //   group A (threads 0..NT-1):    cp.async loads (inputs, and the x/y values B2
 //                                 needs), F1(t), B1(t-2)
@@ -470,8 +472,9 @@ namespace fssim {
 // Group B keeps, per row, the last 10 columns of the F1 output and of the B1
 // output in registers, as two 8-column blocks used in turn (its loop covers two
 // slots per iteration, so only 2 carried columns are copied per slot).
-// Unrolling further (5 slots, to index 40-column rings at compile time) was
-// measured slower: the larger body misses the instruction cache.
+// Unrolling further (5 slots, to index 40-column rings at compile time), or
+// fusing F1 and B1 into one loop, was measured slower: the larger body misses
+// the instruction cache.
 // ---------------------------------------------------------------------------
 
 template <int NT>
