@@ -75,6 +75,14 @@ KInfo kinfo()
                  fssim::Geo<NT>::S, NT};
 }
 
+// Forward two-group pipeline (Float32 inputs, images below 2^31 elements).
+template <int NT>
+KInfo fpinfo()
+{
+    return KInfo{reinterpret_cast<const void*>(&fssim::fwd_pipe_kernel<NT>), fssim::FPGeo<NT>::total, NT,
+                 fssim::FPGeo<NT>::S, 2 * NT};
+}
+
 template <int NT, bool WS, int IOM>
 KInfo pinfo()
 {
@@ -128,7 +136,7 @@ KInfo finfo()
 // Gradients run the two-group pipelined kernel (32-bit in-image offsets: the
 // caller guarantees C*H*W < 2^31); forward-only SSIM on Float32 inputs runs the
 // single-group streaming kernel (or tiles, see use_tiles).
-KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io, int iom)
+KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io, int iom, bool small_image)
 {
     if (fused) {
         switch (f32io ? 0 : iom) {
@@ -139,6 +147,11 @@ KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io, int iom)
         }
     }
     (void)f32io;   // converted inputs run forward-only as tiles (see use_tiles)
+    if (small_image) {   // 32-bit in-image offsets
+        if (nt == 64) return fpinfo<64>();
+        if (nt == 96) return fpinfo<96>();
+        return fpinfo<128>();
+    }
     if (nt == 64) return kinfo<64>();
     if (nt == 96) return kinfo<96>();
     return kinfo<128>();
@@ -257,7 +270,7 @@ int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f
             g.nb = static_cast<int>(nb);
         }
     }
-    g.ki = kernel_info(g.nt, g.fused, g.want_ssim, f32io, iom);
+    g.ki = kernel_info(g.nt, g.fused, g.want_ssim, f32io, iom, c * h * w < (int64_t(1) << 31));
     int sms = 0, occ = 0;
     int st = device_facts(g.ki, &sms, &occ);
     if (st != FSSIM_OK) return st;

@@ -104,7 +104,8 @@ __device__ __forceinline__ bool in_bounds(int64_t idx, int64_t limit, unsigned s
 // Site numbers reported by the bounds-checked build.
 enum BoundsSite : unsigned {
     SITE_BAND_LOAD = 1, SITE_PIPE_STAGE, SITE_PIPE_XY, SITE_PIPE_STAGE_RAW, SITE_PIPE_XY_RAW,
-    SITE_PIPE_GRAD, SITE_TILE_LOAD, SITE_F64_LOAD, SITE_F64_GRAD, SITE_PARTIALS, SITE_COUNTERS
+    SITE_PIPE_GRAD, SITE_TILE_LOAD, SITE_F64_LOAD, SITE_F64_GRAD, SITE_PARTIALS, SITE_COUNTERS,
+    SITE_FPIPE_STAGE
 };
 
 // Raw bits of one input element (zero-extended); converted at staging time so
@@ -895,6 +896,213 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
         const int local_cta = (band * p.nseg + seg) * p.C + c;
         finish_image<2 * NT>(p, n, local_cta, tsum, red);
     }
+}
+
+}  // namespace fssim
+
+namespace fssim {
+
+// ---------------------------------------------------------------------------
+// Two-group pipelined forward kernel (SSIM only, Float32 inputs): the forward
+// half of pipe_kernel.  Group A loads step t+1 with cp.async and runs F1(t);
+// group B runs F2(t-1) and the SSIM map.  One barrier per slot; the F1 output
+// and the staging tile are double-buffered by slot parity; group B keeps the
+// F1 history of its row as two 8-column blocks used in turn.  In-image offsets
+// are 32-bit (the host routes images of 2^31 elements or more elsewhere).
+// ---------------------------------------------------------------------------
+template <int NT>
+struct FPGeo {
+    static constexpr int S = 8;
+    static constexpr int R1 = NT, T = NT, R2 = NT + 2 * RAD, LAG = RAD;
+    static constexpr int SP = S + 1, FC = S + 1;
+    static constexpr int LROWS = (R2 + NT - 1) / NT;
+    static constexpr int stage_one = R2 * SP * 8;
+    static constexpr int f1_one = R1 * FC * 16;
+    static constexpr int red_bytes = (2 * NT / 32 + 2) * 8;
+    static constexpr int off_stage = 0;
+    static constexpr int off_f1 = off_stage + 2 * stage_one;
+    static constexpr int off_red = off_f1 + 2 * f1_one;
+    static constexpr int total = off_red + red_bytes;
+    static_assert(R1 % V == 0 && NT % 32 == 0 && S * (R1 / V) == NT, "F1 items = one per thread");
+    static_assert(stage_one % 16 == 0 && f1_one % 16 == 0, "16-byte alignment of the buffers");
+};
+
+template <int NT>
+__global__ void __launch_bounds__(2 * NT, 512 / (2 * NT)) fwd_pipe_kernel(const Params p)
+{
+    using G = FPGeo<NT>;
+    constexpr int S = G::S, R1 = G::R1, T = G::T, R2 = G::R2, LAG = G::LAG;
+    constexpr int SP = G::SP, FC = G::FC;
+    constexpr int STG = R2 * SP, F1N = R1 * FC;
+
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    float2* stage = reinterpret_cast<float2*>(smem_raw + G::off_stage);
+    float4* f1buf = reinterpret_cast<float4*>(smem_raw + G::off_f1);
+    double* red = reinterpret_cast<double*>(smem_raw + G::off_red);
+
+    const int tid = threadIdx.x;
+    int64_t blk = blockIdx.x;
+    const int c = static_cast<int>(blk % p.C);
+    blk /= p.C;
+    const int seg = static_cast<int>(blk % p.nseg);
+    blk /= p.nseg;
+    const int band = static_cast<int>(blk % p.nb);
+    const int n = static_cast<int>(blk / p.nb);
+    const int C = p.C, H = p.H, W = p.W;
+    const int h0 = band * T;
+    const int w0 = seg * p.L;
+    const int wend = min(w0 + p.L, W);
+    const int Lc = wend - w0;
+    const int64_t ibase = static_cast<int64_t>(n) * p.img_elems + c;
+    const float* __restrict__ xg = reinterpret_cast<const float*>(p.x) + ibase;
+    const float* __restrict__ yg = reinterpret_cast<const float*>(p.y) + ibase;
+    const uint32_t CH32 = static_cast<uint32_t>(C) * static_cast<uint32_t>(H);
+    const int ns = (Lc + 2 * LAG - 1) / S + 1;       // steps of the stream
+    const int nslot = (ns + 2) & ~1;                 // F2 lags one slot; even for the 2-slot loop
+
+    float2 KP[RAD + 1];
+#pragma unroll
+    for (int i = 0; i <= RAD; ++i) KP[i] = make_float2(p.kh[i], p.kh[i]);
+#define FSSIM_K2(tap) KP[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
+
+    // group B's first slot reads F1 output that does not exist yet: zeros
+    for (int e = tid; e < 2 * F1N; e += 2 * NT) f1buf[e] = make_float4(0.f, 0.f, 0.f, 0.f);
+    __syncthreads();
+    double tsum = 0.0;
+
+    if (tid < NT) {
+        // ================= group A: loads, F1 =================
+        const int ta = tid;
+        const int j1 = ta & (S - 1), q1 = ta >> 3;
+        uint32_t lrow_off[G::LROWS];
+        bool lrow_ok[G::LROWS];
+#pragma unroll
+        for (int r = 0; r < G::LROWS; ++r) {
+            const int i = ta + NT * r;
+            const int hr = h0 - LAG + i;
+            lrow_ok[r] = i < R2 && hr >= 0 && hr < H;
+            lrow_off[r] = static_cast<uint32_t>(C) * static_cast<uint32_t>(lrow_ok[r] ? hr : 0);
+        }
+        auto issue_stage = [&](int k, float2* buf) {   // stage <- input columns of step k
+            const int cb = w0 - LAG + k * S;
+#pragma unroll
+            for (int j = 0; j < S; ++j) {
+                const int wc = cb + j;
+                const bool colok = static_cast<unsigned>(wc) < static_cast<unsigned>(W);
+                const uint32_t coloff = CH32 * static_cast<uint32_t>(colok ? wc : 0);
+#pragma unroll
+                for (int r = 0; r < G::LROWS; ++r) {
+                    const int i = ta + NT * r;
+                    if (G::LROWS == 1 || i < R2) {
+                        const uint32_t off = lrow_off[r] + coloff;
+                        const bool ok = lrow_ok[r] && colok &&
+                                        FSSIM_IN_BOUNDS(ibase + off, p.total_elems, SITE_FPIPE_STAGE);
+                        cp_async4(&buf[i * SP + j].x, xg + off, ok);
+                        cp_async4(&buf[i * SP + j].y, yg + off, ok);
+                    }
+                }
+            }
+        };
+        issue_stage(0, stage);
+        cp_async_commit();
+        cp_async_wait<0>();
+        __syncthreads();
+#pragma unroll 1
+        for (int t = 0; t < nslot; ++t) {
+            if (t + 1 < ns) issue_stage(t + 1, stage + ((t + 1) & 1) * STG);
+            cp_async_commit();
+            if (t < ns) {   // -------- F1(t): h-direction pass of the 4 moment images --------
+                const float2* st = stage + (t & 1) * STG;
+                float4* f1 = f1buf + (t & 1) * F1N;
+                float2 aA[V], aB[V];
+#pragma unroll
+                for (int o = 0; o < V; ++o) {
+                    aA[o] = make_float2(0.f, 0.f);
+                    aB[o] = make_float2(0.f, 0.f);
+                }
+#pragma unroll
+                for (int i = 0; i < V + 2 * RAD; ++i) {
+                    const float2 xy = st[(V * q1 + i) * SP + j1];
+                    const float2 sq = __fmul2_rn(xy, xy);                     // (x^2, y^2)
+                    const float2 sb = make_float2(sq.x + sq.y, xy.x * xy.y);  // (x^2+y^2, xy)
+#pragma unroll
+                    for (int o = 0; o < V; ++o) {
+                        const int tap = i - o;
+                        if (tap >= 0 && tap < TAPS) {
+                            aA[o] = __ffma2_rn(xy, FSSIM_K2(tap), aA[o]);
+                            aB[o] = __ffma2_rn(sb, FSSIM_K2(tap), aB[o]);
+                        }
+                    }
+                }
+#pragma unroll
+                for (int o = 0; o < V; ++o)
+                    f1[(V * q1 + o) * FC + j1] = make_float4(aA[o].x, aA[o].y, aB[o].x, aB[o].y);
+            }
+            cp_async_wait<0>();
+            __syncthreads();
+        }
+    } else {
+        // ================= group B: F2 + SSIM map =================
+        const int tb = tid - NT;
+        const bool row_owned = h0 + tb < H;
+        static_assert(HIST == S + 2, "window = 2 saved columns + previous block + current block");
+        float2 A0[S], A1[S], B0[S], B1[S], TA[2], TB[2];
+#pragma unroll
+        for (int m = 0; m < S; ++m) A0[m] = A1[m] = B0[m] = B1[m] = make_float2(0.f, 0.f);
+        TA[0] = TA[1] = TB[0] = TB[1] = make_float2(0.f, 0.f);
+        auto bslot = [&](int t, float2(&Acur)[S], float2(&Aprv)[S], float2(&Bcur)[S], float2(&Bprv)[S]) {
+            const int k = t - 1;   // F2 of step k (k = -1 reads the zeroed buffer)
+            const float4* f1 = f1buf + (k & 1) * F1N;
+            const int wcb = w0 - LAG + k * S - RAD;   // image column of output o = 0
+            float ssum = 0.f;
+#define FSSIM_WA(m) ((m) < 2 ? TA[(m)] : ((m) < HIST ? Aprv[(m) - 2] : Acur[(m) - HIST]))
+#define FSSIM_WB(m) ((m) < 2 ? TB[(m)] : ((m) < HIST ? Bprv[(m) - 2] : Bcur[(m) - HIST]))
+#pragma unroll
+            for (int o = 0; o < S; ++o) {
+                {   // column o of this step enters the window just before its first use
+                    const float4 v = f1[tb * FC + o];
+                    Acur[o] = make_float2(v.x, v.y);
+                    Bcur[o] = make_float2(v.z, v.w);
+                }
+                float2 a = __fmul2_rn(FSSIM_WA(o + RAD), KP[RAD]);
+                float2 b = __fmul2_rn(FSSIM_WB(o + RAD), KP[RAD]);
+#pragma unroll
+                for (int tap = 0; tap < RAD; ++tap) {
+                    a = __ffma2_rn(__fadd2_rn(FSSIM_WA(o + tap), FSSIM_WA(o + 2 * RAD - tap)), KP[tap], a);
+                    b = __ffma2_rn(__fadd2_rn(FSSIM_WB(o + tap), FSSIM_WB(o + 2 * RAD - tap)), KP[tap], b);
+                }
+                const float mx = a.x, my = a.y, qs = b.x, pxy = b.y;
+                const float2 sq = __fmul2_rn(a, a);
+                const float mxy = mx * my;
+                const float sumsq = sq.x + sq.y;
+                const float z = sumsq + p.C1;                    // mx^2 + my^2 + C1
+                const float tt = (qs - sumsq) + p.C2;            // vx + vy + C2
+                const float ax = fmaf(2.f, mxy, p.C1);           // 2 mx my + C1
+                const float by = fmaf(2.f, pxy - mxy, p.C2);     // 2 cov + C2
+                const float s = (ax * by) * rcp_approx(z * tt);
+                const int wc = wcb + o;
+                if (row_owned && static_cast<unsigned>(wc - w0) < static_cast<unsigned>(Lc)) ssum += s;
+            }
+#undef FSSIM_WA
+#undef FSSIM_WB
+            tsum += static_cast<double>(ssum);
+            TA[0] = Aprv[S - 2];
+            TA[1] = Aprv[S - 1];
+            TB[0] = Bprv[S - 2];
+            TB[1] = Bprv[S - 1];
+            __syncthreads();
+        };
+        __syncthreads();
+#pragma unroll 1
+        for (int t = 0; t < nslot; t += 2) {
+            bslot(t, A0, A1, B0, B1);
+            bslot(t + 1, A1, A0, B1, B0);
+        }
+    }
+#undef FSSIM_K2
+
+    const int local_cta = (band * p.nseg + seg) * p.C + c;
+    finish_image<2 * NT>(p, n, local_cta, tsum, red);
 }
 
 }  // namespace fssim

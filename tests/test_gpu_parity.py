@@ -236,3 +236,32 @@ def test_forward_tile_and_streaming_kernels_agree_across_the_threshold(pkg):
     for i in range(3):                                               # 1.47 Mi elements each: tiles
         pkg.ssim_(single, xt[..., i:i + 1], yt[..., i:i + 1])
         assert abs(float(single[0]) - float(whole[i])) <= SSIM_ATOL
+
+
+def test_forward_on_an_image_of_more_than_2_31_elements(pkg, orc):
+    """1 x 46341 x 46341 (2^31 + 4633 elements) runs the 64-bit streaming kernel.  x = y gives
+    SSIM 1; zeroing y's last column changes only the map near it.  The oracle on a crop of the
+    last 22 columns (whose left half is unchanged, so it adds s = 1 exactly) gives the expected
+    shift of the full-image mean; the rounding of the unchanged pixels cancels in the shift."""
+    n = 46341
+    if torch.cuda.get_device_properties(0).total_memory < 40 * 2**30:
+        pytest.skip("needs 2 x 8.6 GB of device memory")
+    g = torch.Generator(device="cuda")
+    g.manual_seed(5)
+    x = pkg.jl_empty((1, n, n, 1), torch.float32)
+    x.uniform_(0.0, 1.0, generator=g)
+    y = x.clone()
+    same = torch.empty(1, dtype=torch.float64, device="cuda")
+    pkg.ssim_(same, x, y)
+    y[0, :, n - 1, 0] = 0.0
+    changed = torch.empty(1, dtype=torch.float64, device="cuda")
+    pkg.ssim_(changed, x, y)
+    k = 22
+    xc, yc = pkg.jl_to_numpy(x[:, :, n - k:, :]), pkg.jl_to_numpy(y[:, :, n - k:, :])
+    del x, y
+    torch.cuda.empty_cache()
+    rc, _ = orc.ssim(xc, yc, flags=orc.SKIP_BACKWARD, precision="f64")
+    shift = (float(rc[0]) - 1.0) * (n * k) / (n * n)
+    assert abs(float(same[0]) - 1.0) <= 1e-6
+    assert shift < -1e-5                                   # the change is visible at this size
+    assert abs((float(changed[0]) - float(same[0])) - shift) <= 1e-9 + 1e-4 * abs(shift)
