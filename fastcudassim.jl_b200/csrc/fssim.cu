@@ -75,12 +75,20 @@ KInfo kinfo()
                  fssim::Geo<NT>::S, NT};
 }
 
-// Forward two-group pipeline (Float32 inputs, images below 2^31 elements).
-template <int NT>
+// Forward two-group pipeline (images below 2^31 elements); IOM as pipe_kernel.
+template <int NT, int IOM>
 KInfo fpinfo()
 {
-    return KInfo{reinterpret_cast<const void*>(&fssim::fwd_pipe_kernel<NT>), fssim::FPGeo<NT>::total, NT,
+    return KInfo{reinterpret_cast<const void*>(&fssim::fwd_pipe_kernel<NT, IOM>), fssim::FPGeo<NT>::total, NT,
                  fssim::FPGeo<NT>::S, 2 * NT};
+}
+
+template <int IOM>
+KInfo fpinfo_nt(int nt)
+{
+    if (nt == 64) return fpinfo<64, IOM>();
+    if (nt == 96) return fpinfo<96, IOM>();
+    return fpinfo<128, IOM>();
 }
 
 template <int NT, bool WS, int IOM>
@@ -112,18 +120,18 @@ KInfo tile_info(bool f32io, int iom)
     return tinfo<fssim::IN_ANY>();
 }
 
-// Forward-only calls on the tile kernel: converted (N0f8 / Float16 / mixed)
-// inputs at every size, since the streaming kernel converting in the loader
-// needed about 200 registers a thread; Float32 inputs up to 4 Mi elements,
-// where a streaming grid needs many short segments (halo warm-up, two warps
-// per CTA).  Measured on B200 (us, tile vs streaming): 1x1080x1920 F32 26.6 vs
-// 30.7, 3x1080x1920 F32 63.5 vs 59.4, 3x1080x1920 N0f8 65.5 vs 85.5,
-// 64x3x512x512 F32 431 vs 324, 64x3x512x512 N0f8 442 vs 545.
-constexpr int64_t kTileMaxF32Elems = int64_t(1) << 22;
+// Forward-only calls up to 4 Mi elements run on the tile kernel: a streaming
+// grid would need many short segments (halo warm-up, few warps per CTA).
+// Larger calls stream (fwd_pipe_kernel), except mixed input dtypes (decoded
+// per element, the streaming loader would spill) and converted inputs in
+// images of 2^31 elements or more, which only the tile kernel reads with
+// 64-bit offsets.
+constexpr int64_t kTileMaxElems = int64_t(1) << 22;
 
-bool use_tiles(int64_t c, int64_t h, int64_t w, int64_t n, bool f32io)
+bool use_tiles(int64_t c, int64_t h, int64_t w, int64_t n, bool f32io, int iom)
 {
-    return !f32io || c * h * w * n <= kTileMaxF32Elems;
+    if (c * h * w * n <= kTileMaxElems) return true;
+    return !f32io && (iom == fssim::IN_ANY || c * h * w >= (int64_t(1) << 31));
 }
 
 template <bool F, bool WS>
@@ -134,8 +142,9 @@ KInfo finfo()
 }
 
 // Gradients run the two-group pipelined kernel (32-bit in-image offsets: the
-// caller guarantees C*H*W < 2^31); forward-only SSIM on Float32 inputs runs the
-// single-group streaming kernel (or tiles, see use_tiles).
+// caller guarantees C*H*W < 2^31); forward-only SSIM runs the two-group forward
+// kernel, or tiles (see use_tiles), or for Float32 images of 2^31 elements or
+// more the single-group streaming kernel.
 KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io, int iom, bool small_image)
 {
     if (fused) {
@@ -146,12 +155,11 @@ KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io, int iom, bool 
             default: return pinfo_io<fssim::IN_ANY>(nt, want_ssim);
         }
     }
-    (void)f32io;   // converted inputs run forward-only as tiles (see use_tiles)
-    if (small_image) {   // 32-bit in-image offsets
-        if (nt == 64) return fpinfo<64>();
-        if (nt == 96) return fpinfo<96>();
-        return fpinfo<128>();
+    if (small_image) {   // 32-bit in-image offsets; mixed dtypes run as tiles (see use_tiles)
+        if (f32io) return fpinfo_nt<0>(nt);
+        return iom == fssim::IN_U8 ? fpinfo_nt<fssim::IN_U8>(nt) : fpinfo_nt<fssim::IN_F16>(nt);
     }
+    // images of 2^31 elements or more: Float32 only (converted inputs run as tiles)
     if (nt == 64) return kinfo<64>();
     if (nt == 96) return kinfo<96>();
     return kinfo<128>();
@@ -234,7 +242,7 @@ int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f
         *cfg = g;
         return FSSIM_OK;
     }
-    if (!g.fused && use_tiles(c, h, w, n, f32io)) {   // small forward-only call: one TH x TW tile per CTA
+    if (!g.fused && use_tiles(c, h, w, n, f32io, iom)) {   // small forward-only call: one TH x TW tile per CTA
         g.ki = tile_info(f32io, iom);
         int sms = 0, occ = 0;
         int st = device_facts(g.ki, &sms, &occ);

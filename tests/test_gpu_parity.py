@@ -265,3 +265,18 @@ def test_forward_on_an_image_of_more_than_2_31_elements(pkg, orc):
     assert abs(float(same[0]) - 1.0) <= 1e-6
     assert shift < -1e-5                                   # the change is visible at this size
     assert abs((float(changed[0]) - float(same[0])) - shift) <= 1e-9 + 1e-4 * abs(shift)
+
+
+@pytest.mark.parametrize("dt", ["u8", "f16"])
+def test_forward_converted_inputs_on_the_streaming_path(pkg, orc, dt):
+    """N0f8 and Float16 forward calls above 4 Mi elements stream (converted in group A's loader)."""
+    shape = (3, 1100, 1400, 1)
+    syn = _syn(pkg)
+    if dt == "u8":
+        x, y = syn.host_pair(37, shape, 0.1, dtype=np.uint8)
+    else:
+        x, y = syn.host_pair(37, shape, 0.1)
+        x, y = np.asfortranarray(x.astype(np.float16)), np.asfortranarray(y.astype(np.float16))
+    v, _ = _run(pkg, x, y, mode="fwd")
+    rv, _ = orc.ssim(x, y, flags=orc.SKIP_BACKWARD, precision="f32")
+    assert np.max(np.abs(v - rv)) <= SSIM_ATOL, (v, rv)
