@@ -124,21 +124,32 @@ def fp32_pipe(kern_s, n_local, clocks, sms):
             "frac": achieved / peak, "clock_mhz": mhz}
 
 
-def cpu_oracle_rate(n_images, nthreads, reps=1):
-    """Gpixel/s of the oracle (reference algorithm, single precision) on host cores."""
-    sys.path.insert(0, os.path.join(ROOT, "oracle"))
-    import oracle
-    import __graft_entry__ as ge
-    syn = __import__(ge.load_package().__name__ + ".synthetic", fromlist=["x"])
-    x, y = syn.host_pair(99, (C, H, W, n_images), NOISE)
-    oracle.ssim(x[..., :1], y[..., :1], nthreads=nthreads)   # warm the library
-    best = None
-    for _ in range(reps):
+class CpuSample:
+    """A sample of the workload on the host (seeded, same distributions) and the
+    oracle (the reference algorithm in single precision, C with pthreads)."""
+
+    def __init__(self, n_images, nthreads):
+        sys.path.insert(0, os.path.join(ROOT, "oracle"))
+        import oracle
+        import __graft_entry__ as ge
+        syn = __import__(ge.load_package().__name__ + ".synthetic", fromlist=["x"])
+        self.oracle, self.n, self.threads = oracle, n_images, nthreads
+        self.x, self.y = syn.host_pair(99, (C, H, W, n_images), NOISE)
+        oracle.ssim(self.x[..., :1], self.y[..., :1], nthreads=nthreads)   # warm the library
+
+    def one_pass(self):
+        """Seconds for SSIM + gradient of the whole sample."""
         t0 = time.perf_counter()
-        oracle.ssim(x, y, nthreads=nthreads)
-        dt = time.perf_counter() - t0
-        best = dt if best is None else min(best, dt)
-    return n_images * H * W / best / 1e9, best
+        self.oracle.ssim(self.x, self.y, nthreads=self.threads)
+        return time.perf_counter() - t0
+
+    def rate(self, min_seconds):
+        """Gpixel/s over as many passes as fill `min_seconds` of CPU time."""
+        passes, spent = 0, 0.0
+        while spent < min_seconds or passes == 0:
+            spent += self.one_pass()
+            passes += 1
+        return passes * self.n * H * W / spent / 1e9, passes, spent
 
 
 def run_reference(args):
@@ -146,13 +157,13 @@ def run_reference(args):
     if rank != 0:
         return 0
     threads = os.cpu_count() or 1
-    sample = max(4, -(-2 * threads // C))      # about two (image, channel) planes per host thread
+    # about one second of work per step: 10 images per host thread (an image with its
+    # gradient takes the oracle about 0.1 s on one core), at most 256 (2.4 GB of host memory)
+    sample = max(4, min(256, 10 * threads))
+    cs = CpuSample(sample, threads)
     for _ in range(args.warmup):
-        cpu_oracle_rate(sample, threads)
-    times = []
-    for _ in range(args.steps):
-        _, dt = cpu_oracle_rate(sample, threads)
-        times.append(dt)
+        cs.one_pass()
+    times = [cs.one_pass() for _ in range(args.steps)]
     t = sum(times)
     value = args.steps * sample * H * W / t / 1e9
     line = {
@@ -297,10 +308,11 @@ def run_ours(args):
         extras = side_benchmarks(pkg, dev)
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
-        n_cpu = 16
-        rate, dt = cpu_oracle_rate(n_cpu, os.cpu_count() or 1)
+        n_cpu = 64
+        rate, passes, spent = CpuSample(n_cpu, os.cpu_count() or 1).rate(min_seconds=10.0)
         cpu = {"value": rate, "unit": "Gpixel/s", "cores": os.cpu_count() or 1, "kind": "port",
-               "sample": f"{n_cpu} images of 3x512x512 with gradient ({dt:.1f} s), oracle in C with pthreads"}
+               "sample": f"{n_cpu} images of 3x512x512 with gradient, {passes} passes ({spent:.1f} s), "
+                         "oracle in C with pthreads"}
 
     if world > 1:
         dist.barrier(device_ids=[local])
