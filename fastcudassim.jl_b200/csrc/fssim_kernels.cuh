@@ -27,9 +27,11 @@
 // the 10+10 warm-up columns of each segment.  Nothing but the inputs, the
 // gradient and one double per CTA ever touches global memory.
 //
-// Kernels: pipe_kernel (SSIM + gradient, two warp groups), band_kernel (forward
-// only, Float32 inputs), tile_fwd_kernel (forward only: small Float32 calls and
-// converted inputs), f64_kernel (any call with a Float64 input).
+// Kernels: pipe_kernel (SSIM + gradient, two warp groups); forward only:
+// fwd_pipe_kernel (its forward half, calls above 4 Mi elements), tile_fwd_kernel
+// (smaller calls, mixed input dtypes) and band_kernel (single group, 64-bit
+// offsets: Float32 images of 2^31 elements or more); f64_kernel (any call with
+// a Float64 input, in double precision).
 //
 // Only four moment images are convolved, not the reference's five: the SSIM map
 // needs the two variances only through their sum, so E[x^2] and E[y^2] are
