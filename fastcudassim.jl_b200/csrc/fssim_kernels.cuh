@@ -258,7 +258,12 @@ __device__ __forceinline__ void finish_image(const Params& p, int n, int local_c
     if (red[NT / 32] != 0.0) {   // uniform over the CTA; no early return, so loops may call this
         __threadfence();
         double v = 0.0;
-        for (int i = threadIdx.x; i < p.cpi; i += NT) v += __ldcg(&p.partials[(int64_t)n * p.cpi + i]);
+        for (int i = threadIdx.x; i < p.cpi; i += NT) {
+            v += __ldcg(&p.partials[(int64_t)n * p.cpi + i]);
+            // leave the workspace zeroed: a later call with more images places its
+            // counters where these partial sums were
+            p.partials[(int64_t)n * p.cpi + i] = 0.0;
+        }
         __syncthreads();   // red[] is reused below
         const double sum = block_sum<NT>(v, red);
         if (threadIdx.x == 0) {

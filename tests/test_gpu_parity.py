@@ -280,3 +280,44 @@ def test_forward_converted_inputs_on_the_streaming_path(pkg, orc, dt):
     v, _ = _run(pkg, x, y, mode="fwd")
     rv, _ = orc.ssim(x, y, flags=orc.SKIP_BACKWARD, precision="f32")
     assert np.max(np.abs(v - rv)) <= SSIM_ATOL, (v, rv)
+
+
+@pytest.mark.parametrize("mode", ["both", "fwd"])
+def test_many_channels(pkg, orc, mode):
+    """C = 16 (a multispectral stack): channels are independent planes averaged per image."""
+    x, y = _syn(pkg).host_pair(43, (16, 45, 38, 2), 0.1)
+    v, g = _run(pkg, x, y, mode=mode)
+    rv, rg = orc.ssim(x, y, flags=0 if mode == "both" else orc.SKIP_BACKWARD, precision="f64")
+    assert np.max(np.abs(v - rv)) <= SSIM_ATOL
+    if g is not None:
+        assert _rel_l2(g, rg) <= GRAD_RTOL_L2
+
+
+@pytest.mark.parametrize("mode", ["both", "fwd"])
+def test_many_tiny_images(pkg, orc, mode):
+    """5000 images of 1 x 9 x 13: one CTA per image, so every image's counter and
+    last-CTA reduction run, thousands at once."""
+    x, y = _syn(pkg).host_pair(47, (1, 9, 13, 5000), 0.2)
+    v, g = _run(pkg, x, y, mode=mode)
+    rv, rg = orc.ssim(x, y, flags=0 if mode == "both" else orc.SKIP_BACKWARD, precision="f64")
+    assert np.max(np.abs(v - rv)) <= SSIM_ATOL
+    if g is not None:
+        assert _rel_l2(g, rg) <= GRAD_RTOL_L2
+    # the workspace is left zeroed: a second call gives the same values
+    v2, _ = _run(pkg, x, y, mode=mode)
+    np.testing.assert_array_equal(v, v2)
+
+
+def test_workspace_reuse_from_few_to_many_images(pkg, orc):
+    """The workspace is shared by the calls on a stream.  A call with few large images writes
+    many per-CTA partial sums just after its counters; a later call with more images places its
+    counters over them.  Every call must leave the workspace zeroed for that to work."""
+    syn = _syn(pkg)
+    xb, yb = syn.host_pair(51, (3, 300, 400, 2), 0.1)          # 2 images, dozens of CTAs each
+    _run(pkg, xb, yb, mode="both")
+    xs, ys = syn.host_pair(53, (1, 20, 20, 200), 0.1)         # 200 counters: bytes 0..799
+    for mode in ("both", "fwd"):
+        v, _ = _run(pkg, xs, ys, mode=mode)
+        rv, _ = orc.ssim(xs, ys, flags=0 if mode == "both" else orc.SKIP_BACKWARD, precision="f64")
+        assert np.max(np.abs(v - rv)) <= SSIM_ATOL, np.argmax(np.abs(v - rv))
+        _run(pkg, xb, yb, mode=mode)
