@@ -67,6 +67,21 @@ def promote_dtype(t1: torch.dtype, t2: torch.dtype) -> torch.dtype:
     return torch.float64 if torch.float64 in (t1, t2) else torch.float32
 
 
+def _span(t: torch.Tensor) -> tuple[int, int]:
+    return t.data_ptr(), t.data_ptr() + t.numel() * t.element_size()
+
+
+def _overlap(a: torch.Tensor, b: torch.Tensor) -> bool:
+    (a0, a1), (b0, b1) = _span(a), _span(b)
+    return a.device == b.device and a0 < b1 and b0 < a1
+
+
+def _jl_copy(t: torch.Tensor) -> torch.Tensor:
+    out = jl_empty(tuple(t.shape), t.dtype, t.device)
+    out.copy_(t)
+    return out
+
+
 def _require_device_array(name: str, t: torch.Tensor) -> None:
     if not isinstance(t, torch.Tensor):
         raise TypeError(f"{name} must be a torch.Tensor in Julia (column-major) layout")
@@ -143,6 +158,13 @@ def ssim_fwd_bwd(ssims, dL_dimgs1, imgs1, imgs2, N_dssims_dQMP, should_zero: boo
         flags |= nat.USE_DSSIM
         if divide_by_two_in_dssim:
             flags |= nat.DIVIDE_BY_TWO
+    if dl_c is not None:
+        # The gradient may be asked for in an input's own buffer (the reference's separate
+        # backward launch allows it); the fused kernel does not, so that input is copied.
+        if _overlap(dl_c, cimgs1):
+            cimgs1 = _jl_copy(cimgs1)
+        if _overlap(dl_c, cimgs2):
+            cimgs2 = _jl_copy(cimgs2)
     if grad_scale is not None and not skip_backward:
         if tuple(grad_scale.shape) not in ((b,), ()) or (grad_scale.ndim == 0 and b != 1):
             raise nat.DimensionMismatch(

@@ -316,6 +316,11 @@ bool is_input_dtype(int d)
 bool is_float_dtype(int d) { return d == FSSIM_FLOAT32 || d == FSSIM_FLOAT16 || d == FSSIM_FLOAT64; }
 size_t dsize(int d) { return d == FSSIM_FLOAT32 ? 4 : d == FSSIM_FLOAT16 ? 2 : d == FSSIM_N0F8 ? 1 : 8; }
 bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+bool overlaps(const void* a, size_t an, const void* b, size_t bn)
+{
+    const uintptr_t a0 = reinterpret_cast<uintptr_t>(a), b0 = reinterpret_cast<uintptr_t>(b);
+    return a0 < b0 + bn && b0 < a0 + an;
+}
 
 int check_sizes(int64_t c, int64_t h, int64_t w, int64_t n)
 {
@@ -434,6 +439,24 @@ int fwd_bwd_impl(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs
             return fail(FSSIM_ERR_MISALIGNED, "dL_dimgs1 must be aligned to its element size");
     }
     if (!want_ssim && !fused) return ok();   // nothing requested
+
+    // The outputs must not share memory with the inputs: CTAs read input rows of
+    // their neighbours' bands (the halo) after other CTAs have written outputs.
+    // (The reference's separate backward launch tolerated dL_dimgs1 === imgs1;
+    // the host layer copies an aliased input instead.)
+    {
+        const size_t elems = static_cast<size_t>(c * h * w * n);
+        const size_t xb = elems * dsize(imgs1_dtype), yb = elems * dsize(imgs2_dtype);
+        if (fused && (overlaps(dL_dimgs1, elems * dsize(grad_dtype), imgs1, xb) ||
+                      overlaps(dL_dimgs1, elems * dsize(grad_dtype), imgs2, yb)))
+            return fail(FSSIM_ERR_INVALID_ARGUMENT, "dL_dimgs1 overlaps imgs1 or imgs2; pass a copy of the input");
+        if (want_ssim && (overlaps(ssims, static_cast<size_t>(n) * dsize(ssims_dtype), imgs1, xb) ||
+                          overlaps(ssims, static_cast<size_t>(n) * dsize(ssims_dtype), imgs2, yb)))
+            return fail(FSSIM_ERR_INVALID_ARGUMENT, "ssims overlaps imgs1 or imgs2");
+        if (want_ssim && fused &&
+            overlaps(ssims, static_cast<size_t>(n) * dsize(ssims_dtype), dL_dimgs1, elems * dsize(grad_dtype)))
+            return fail(FSSIM_ERR_INVALID_ARGUMENT, "ssims overlaps dL_dimgs1");
+    }
 
     if (fused && c * h * w >= (int64_t(1) << 31))
         return fail(FSSIM_ERR_INVALID_ARGUMENT, "gradient calls need C*H*W < 2^31 elements per image (got %lld)",

@@ -110,6 +110,11 @@ int fssim_workspace_size(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t fl
  *               interface parity and never read or written: the fused kernel keeps
  *               the partial gradients on chip.  May be NULL.
  *  workspace    >= fssim_workspace_size() bytes, zero-filled before first use.
+ *
+ * The outputs (ssims, dL_dimgs1) must not overlap the inputs or each other
+ * (FSSIM_ERR_INVALID_ARGUMENT): the fused kernel reads input rows around its
+ * band after other blocks have written their outputs.  A caller that wants the
+ * gradient in imgs1's own buffer copies imgs1 first.
  */
 int fssim_fwd_bwd(void* ssims, int ssims_dtype, int64_t ssims_len,
                   void* dL_dimgs1, int grad_dtype,

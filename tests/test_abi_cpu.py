@@ -87,3 +87,17 @@ def test_bounds_status_needs_the_checked_build(pkg):
     st = lib.fssim_debug_bounds_status(ctypes.byref(site), ctypes.byref(count), 0)
     assert st == pkg._native.ERR_INVALID_ARGUMENT
     assert "FSSIM_DEBUG_BOUNDS" in pkg._native.last_error()[1]
+
+
+def test_outputs_overlapping_inputs_are_refused(pkg):
+    """Checked before any CUDA call: 1 x 8 x 8 x 1 Float32 arrays span 256 bytes."""
+    lib = pkg._native.load()
+    nat = pkg._native
+    x, y = 1 << 20, 1 << 21
+    for grad in (x, x + 128, y - 128):
+        st = lib.fssim_fwd_bwd(None, 0, 1, ctypes.c_void_p(grad), 0, ctypes.c_void_p(x), 0, ctypes.c_void_p(y), 0,
+                               None, 1, 8, 8, 1, nat.SKIP_SSIM, None, 0, None)
+        assert st == nat.ERR_INVALID_ARGUMENT and "overlaps" in nat.last_error()[1]
+    st = lib.fssim_fwd_bwd(ctypes.c_void_p(y + 64), 0, 1, None, 0, ctypes.c_void_p(x), 0, ctypes.c_void_p(y), 0,
+                           None, 1, 8, 8, 1, nat.SKIP_BACKWARD, None, 0, None)
+    assert st == nat.ERR_INVALID_ARGUMENT and "overlaps" in nat.last_error()[1]

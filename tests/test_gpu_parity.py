@@ -321,3 +321,23 @@ def test_workspace_reuse_from_few_to_many_images(pkg, orc):
         rv, _ = orc.ssim(xs, ys, flags=0 if mode == "both" else orc.SKIP_BACKWARD, precision="f64")
         assert np.max(np.abs(v - rv)) <= SSIM_ATOL, np.argmax(np.abs(v - rv))
         _run(pkg, xb, yb, mode=mode)
+
+
+def test_gradient_into_the_first_input_buffer(pkg, orc):
+    """`ssim_gradient!(imgs1, imgs1, imgs2, nothing)` works in the reference (its backward
+    launch reads x only at the pixel it writes).  The fused kernel reads neighbouring rows
+    late, so the driver copies the aliased input; the C ABI refuses the overlap itself."""
+    x, y = _syn(pkg).host_pair(57, (3, 150, 120, 2), 0.1)
+    xt, yt = pkg.jl_from_numpy(x), pkg.jl_from_numpy(y)
+    buf = xt.data_ptr()
+    g = pkg.ssim_gradient_(xt, xt, yt, None)
+    torch.cuda.synchronize()
+    assert g.data_ptr() == buf
+    _, rg = orc.ssim(x, y, precision="f64")
+    assert _rel_l2(pkg.jl_to_numpy(xt), rg) <= GRAD_RTOL_L2
+    # the same with DSSIM/2 and the gradient written into imgs2's buffer
+    x2, y2 = pkg.jl_from_numpy(x), pkg.jl_from_numpy(y)
+    pkg.dssim_gradient_(y2, x2, y2, None, True)
+    torch.cuda.synchronize()
+    _, rg2 = orc.ssim(x, y, flags=orc.USE_DSSIM | orc.DIVIDE_BY_TWO, precision="f64")
+    assert _rel_l2(pkg.jl_to_numpy(y2), rg2) <= GRAD_RTOL_L2
