@@ -124,6 +124,23 @@ def fp32_pipe(kern_s, n_local, clocks, sms):
             "frac": achieved / peak, "clock_mhz": mhz}
 
 
+def cpu_fullhd_ms(channels, reps=3):
+    """The oracle's forward SSIM on one full-HD pair (ms, best of `reps`).  The oracle
+    parallelises over (image, channel) planes, so it uses `channels` host threads."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    import __graft_entry__ as ge
+    syn = __import__(ge.load_package().__name__ + ".synthetic", fromlist=["x"])
+    x, y = syn.host_pair(7, (channels, 1080, 1920, 1), NOISE)
+    best = None
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        oracle.ssim(x, y, flags=oracle.SKIP_BACKWARD, nthreads=channels)
+        dt = (time.perf_counter() - t0) * 1e3
+        best = dt if best is None else min(best, dt)
+    return best
+
+
 class CpuSample:
     """A sample of the workload on the host (seeded, same distributions) and the
     oracle (the reference algorithm in single precision, C with pthreads)."""
@@ -306,6 +323,10 @@ def run_ours(args):
     extras = {}
     if rank == 0 and not args.no_extras:
         extras = side_benchmarks(pkg, dev)
+        if not args.no_cpu:   # the same full-HD SSIM on host cores (one thread per channel plane)
+            extras["cpu_fullhd_1ch_ssim_ms"] = cpu_fullhd_ms(1)
+            extras["cpu_fullhd_3ch_ssim_ms"] = cpu_fullhd_ms(3)
+            extras["cpu_fullhd_cores"] = {"1ch": 1, "3ch": 3}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         n_cpu = 64
