@@ -6,6 +6,7 @@ statically, so the library only needs the NVIDIA driver at run time.
 """
 from __future__ import annotations
 
+import glob
 import os
 import subprocess
 import sys
@@ -13,7 +14,7 @@ import sys
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
 SRC = [os.path.join(HERE, "csrc", "fssim.cu")]
-DEPS = SRC + [os.path.join(HERE, "csrc", "fssim_kernels.cuh"), os.path.join(ROOT, "include", "fastssim.h")]
+DEPS = SRC + sorted(glob.glob(os.path.join(HERE, "csrc", "*.cuh"))) + [os.path.join(ROOT, "include", "fastssim.h")]
 OUT = os.path.join(HERE, "lib", "libfastssim.so")
 # The same sources with every global access bounds-checked (tests only).
 OUT_BOUNDS = os.path.join(HERE, "lib", "libfastssim_bounds.so")
