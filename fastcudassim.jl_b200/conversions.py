@@ -16,10 +16,14 @@ import torch
 
 
 def is_column_major(t: torch.Tensor) -> bool:
-    """True if ``t`` is laid out like a Julia array of size ``t.shape``."""
-    if t.ndim <= 1:
-        return t.ndim == 0 or t.stride(0) == 1 or t.shape[0] <= 1
-    return t.permute(*reversed(range(t.ndim))).is_contiguous()
+    """True if ``t`` is laid out like a Julia array of size ``t.shape`` (dimensions of
+    size 1 may have any stride)."""
+    expect = 1
+    for size, stride in zip(t.shape, t.stride()):
+        if size != 1 and stride != expect:
+            return False
+        expect *= size
+    return True
 
 
 def jl_empty(shape, dtype=torch.float32, device="cuda") -> torch.Tensor:
@@ -50,9 +54,16 @@ def jl_reshape(t: torch.Tensor, shape) -> torch.Tensor:
     shape = tuple(int(s) for s in shape)
     if not is_column_major(t):
         raise ValueError("jl_reshape needs a column-major (Julia-layout) tensor")
-    rev = t.permute(*reversed(range(t.ndim)))
-    out = rev.view(tuple(reversed(shape)))
-    return out.permute(*reversed(range(len(shape))))
+    n = 1
+    for s in shape:
+        n *= s
+    if n != t.numel():
+        raise ValueError(f"cannot reshape an array of {t.numel()} elements to size {shape}")
+    strides, acc = [], 1
+    for s in shape:
+        strides.append(acc)
+        acc *= s
+    return t.as_strided(shape, tuple(strides))
 
 
 def canonicalize_image(img: torch.Tensor) -> torch.Tensor:

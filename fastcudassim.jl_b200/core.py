@@ -41,10 +41,19 @@ def _workspace_size(c: int, h: int, w: int, n: int, flags: int, device_index: in
     return nbytes
 
 
-def _workspace(device: torch.device, stream: torch.cuda.Stream, nbytes: int) -> torch.Tensor | None:
+def _current_stream_handle(device_index: int) -> int:
+    """The raw cudaStream_t of the current stream of a device (without building a
+    torch Stream object on every call)."""
+    raw = getattr(torch._C, "_cuda_getCurrentRawStream", None)
+    if raw is not None:
+        return int(raw(device_index))
+    return torch.cuda.current_stream(device_index).cuda_stream
+
+
+def _workspace(device: torch.device, stream: int, nbytes: int) -> torch.Tensor | None:
     if nbytes == 0:
         return None
-    key = (device.index, stream.cuda_stream)
+    key = (device.index, stream)
     with _ws_lock:
         ws = _workspaces.get(key)
         if ws is None or ws.numel() < nbytes:
@@ -186,7 +195,7 @@ def ssim_fwd_bwd(ssims, dL_dimgs1, imgs1, imgs2, N_dssims_dQMP, should_zero: boo
     if switch:
         torch.cuda.set_device(device)
     try:
-        stream = torch.cuda.current_stream(device)
+        stream = _current_stream_handle(device.index)
         nbytes = _workspace_size(c, h, w, b, flags, device.index)
         ws = _workspace(device, stream, nbytes)
         out_args = (ssims.data_ptr() if not skip_ssim else 0, dtype_code(ssims) if not skip_ssim else nat.FLOAT32,
@@ -194,8 +203,7 @@ def ssim_fwd_bwd(ssims, dL_dimgs1, imgs1, imgs2, N_dssims_dQMP, should_zero: boo
                     dl_c.data_ptr() if dl_c is not None else 0,
                     dtype_code(dl_c) if dl_c is not None else nat.FLOAT32,
                     cimgs1.data_ptr(), dtype_code(cimgs1), cimgs2.data_ptr(), dtype_code(cimgs2))
-        ws_args = (ws.data_ptr() if ws is not None else 0, ws.numel() if ws is not None else 0,
-                   stream.cuda_stream)
+        ws_args = (ws.data_ptr() if ws is not None else 0, ws.numel() if ws is not None else 0, stream)
         if grad_scale is None:
             nat.fwd_bwd(*out_args, 0, c, h, w, b, flags, *ws_args)
         else:
