@@ -341,3 +341,35 @@ def test_gradient_into_the_first_input_buffer(pkg, orc):
     torch.cuda.synchronize()
     _, rg2 = orc.ssim(x, y, flags=orc.USE_DSSIM | orc.DIVIDE_BY_TWO, precision="f64")
     assert _rel_l2(pkg.jl_to_numpy(y2), rg2) <= GRAD_RTOL_L2
+
+
+MANY_ROWS_SHAPES = [("1x300x40x600", (1, 300, 40, 600)), ("3x120x60x400", (3, 120, 60, 400))]
+
+
+@pytest.mark.parametrize("name,shape", MANY_ROWS_SHAPES, ids=[s[0] for s in MANY_ROWS_SHAPES])
+@pytest.mark.parametrize("mode,dssim,div2", [("both", False, False), ("both", True, True), ("grad", False, False)])
+def test_many_narrow_band_rows_vs_oracle(pkg, orc, name, shape, mode, dssim, div2):
+    """Thousands of narrow band rows (3600 CTAs, several waves): SSIM, DSSIM/2 and the gradient
+    alone, and bitwise determinism."""
+    x, y = _syn(pkg).host_pair(59, shape, 0.1)
+    v, g = _run(pkg, x, y, mode=mode, dssim=dssim, div2=div2)
+    rv, rg = orc.ssim(x, y, flags=_flags(orc, dssim, div2), precision="f64")
+    if v is not None:
+        assert np.max(np.abs(v - rv)) <= SSIM_ATOL, np.argmax(np.abs(v - rv))
+    assert _rel_l2(g, rg) <= GRAD_RTOL_L2
+    if mode == "both":                      # bitwise deterministic here too
+        v2, g2 = _run(pkg, x, y, mode=mode, dssim=dssim, div2=div2)
+        np.testing.assert_array_equal(v, v2)
+        np.testing.assert_array_equal(g, g2)
+
+
+def test_many_narrow_band_rows_with_gradient_factor(pkg, orc):
+    shape = (1, 300, 40, 600)
+    x, y = _syn(pkg).host_pair(61, shape, 0.1)
+    xt, yt = pkg.jl_from_numpy(x), pkg.jl_from_numpy(y)
+    scale = torch.linspace(-2.0, 2.0, shape[3], device="cuda")
+    _, g = pkg.ssim_fwd_bwd(None, None, xt, yt, None, False, True, False, False, False, grad_scale=scale)
+    torch.cuda.synchronize()
+    _, rg = orc.ssim(x, y, precision="f64")
+    want = rg * scale.double().cpu().numpy().reshape(1, 1, 1, -1)
+    assert _rel_l2(pkg.jl_to_numpy(g), want) <= GRAD_RTOL_L2
