@@ -328,7 +328,8 @@ int check_sizes(int64_t c, int64_t h, int64_t w, int64_t n)
         return fail(FSSIM_ERR_INVALID_ARGUMENT, "sizes must be positive, got (c,h,w,n) = (%lld,%lld,%lld,%lld)",
                     (long long)c, (long long)h, (long long)w, (long long)n);
     const int64_t lim = (int64_t(1) << 31) - 1;
-    if (c > lim || h > lim || w > lim || n > lim || c * h > lim || c * h * w > (int64_t(1) << 40))
+    if (c > lim || h > lim || w > lim || n > lim || c * h > lim || c * h * w > (int64_t(1) << 40) ||
+        c * h * w > (int64_t(1) << 62) / n)   // the element count stays far inside int64
         return fail(FSSIM_ERR_INVALID_ARGUMENT, "sizes out of range (c,h,w,n) = (%lld,%lld,%lld,%lld)",
                     (long long)c, (long long)h, (long long)w, (long long)n);
     return FSSIM_OK;
@@ -478,6 +479,10 @@ int fwd_bwd_impl(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs
                         workspace ? workspace_bytes : (size_t)0);
         if (!aligned(workspace, 256)) return fail(FSSIM_ERR_MISALIGNED, "workspace must be 256-byte aligned");
     }
+
+    if (g.grid > (int64_t(1) << 31) - 1)
+        return fail(FSSIM_ERR_INVALID_ARGUMENT, "%lld thread blocks needed, more than one launch allows; split the batch",
+                    (long long)g.grid);
 
     fssim::Params p{};
     p.x = imgs1;

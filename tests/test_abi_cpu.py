@@ -101,3 +101,15 @@ def test_outputs_overlapping_inputs_are_refused(pkg):
     st = lib.fssim_fwd_bwd(ctypes.c_void_p(y + 64), 0, 1, None, 0, ctypes.c_void_p(x), 0, ctypes.c_void_p(y), 0,
                            None, 1, 8, 8, 1, nat.SKIP_BACKWARD, None, 0, None)
     assert st == nat.ERR_INVALID_ARGUMENT and "overlaps" in nat.last_error()[1]
+
+
+def test_absurd_sizes_are_refused_before_any_cuda_call(pkg):
+    lib = pkg._native.load()
+    nat = pkg._native
+    x = ctypes.c_void_p(1 << 20)
+    size = ctypes.c_size_t(0)
+    # element count beyond int64 headroom: c*h*w = 2^40, n = 2^30
+    assert lib.fssim_workspace_size(1, 1 << 20, 1 << 20, 1 << 30, 0, ctypes.byref(size)) == nat.ERR_INVALID_ARGUMENT
+    st = lib.fssim_fwd_bwd(None, 0, 1, None, 0, x, 0, x, 0, None, 1, 1 << 20, 1 << 20, 1 << 30,
+                           nat.SKIP_SSIM | nat.SKIP_BACKWARD, None, 0, None)
+    assert st == nat.ERR_INVALID_ARGUMENT and "out of range" in nat.last_error()[1]
