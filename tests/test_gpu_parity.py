@@ -1,6 +1,6 @@
 """Parity of the CUDA path (through the C ABI) with the CPU oracle on seeded inputs.
 
-Tolerances: per-image (D)SSIM within 1e-5 absolute; the
+Tolerances (the parity bar): per-image (D)SSIM within 1e-5 absolute; the
 gradient within 1e-4 relative L2, against the single-precision oracle (the
 reference's operation order) and against the float64 oracle.
 """
