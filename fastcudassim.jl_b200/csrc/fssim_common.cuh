@@ -86,7 +86,7 @@ __device__ __forceinline__ float rcp_approx(float v)
 }
 
 // Opt-in bounds checking (built with -DFSSIM_DEBUG_BOUNDS, the library's stand-in
-// for a memory checker): every global access first checks its element index
+// for a memory-error tool): every global access first checks its element index
 // against the array it addresses.  An index out of range is recorded (the first
 // failing site and a count) and the access is skipped instead of made.
 #ifdef FSSIM_DEBUG_BOUNDS

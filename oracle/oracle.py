@@ -1,6 +1,6 @@
 """ctypes front end of the CPU oracle (``liboracle_ssim.so``, built from ``ssim_oracle.c``).
 
-TEST INFRASTRUCTURE ONLY.  This module is the checker for the parity tests, the
+TEST INFRASTRUCTURE ONLY.  This module gives the reference values for the parity tests, the
 ``smoke()`` check and the CPU-baseline leg of ``bench.py``.  Product code never
 imports it.
 

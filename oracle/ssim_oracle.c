@@ -1,8 +1,8 @@
 /*
  * CPU oracle for the SSIM / DSSIM forward pass and the gradient with respect to
  * the first image batch.  TEST INFRASTRUCTURE ONLY: the parity tests, the smoke
- * check and the CPU-baseline leg of the benchmark load this file's library as
- * the checker.  No product code path may call it.
+ * check and the CPU-baseline leg of the benchmark load this file's library for
+ * reference values.  No product code path may call it.
  *
  * It restates the arithmetic of FastCUDASSIM.jl v0.2.1, src/core.jl, in two modes:
  *
