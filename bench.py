@@ -141,6 +141,23 @@ def cpu_fullhd_ms(channels, reps=3):
     return best
 
 
+def cpu_batch32_dssim_grad_ms(nthreads, reps=2):
+    """The oracle's DSSIM + gradient on the 32x3x256x256 batch (ms, best of `reps`) with
+    `nthreads` host threads (it parallelises over the 96 channel planes)."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    import __graft_entry__ as ge
+    syn = __import__(ge.load_package().__name__ + ".synthetic", fromlist=["x"])
+    x, y = syn.host_pair(11, (3, 256, 256, 32), None)
+    best = None
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        oracle.ssim(x, y, flags=oracle.USE_DSSIM, nthreads=nthreads)
+        dt = (time.perf_counter() - t0) * 1e3
+        best = dt if best is None else min(best, dt)
+    return best
+
+
 class CpuSample:
     """A sample of the workload on the host (seeded, same distributions) and the
     oracle (the reference algorithm in single precision, C with pthreads)."""
@@ -327,6 +344,9 @@ def run_ours(args):
             extras["cpu_fullhd_1ch_ssim_ms"] = cpu_fullhd_ms(1)
             extras["cpu_fullhd_3ch_ssim_ms"] = cpu_fullhd_ms(3)
             extras["cpu_fullhd_cores"] = {"1ch": 1, "3ch": 3}
+            ncores = os.cpu_count() or 1
+            extras["cpu_batch32_3x256x256_dssim_grad_ms"] = {"1": cpu_batch32_dssim_grad_ms(1),
+                                                             str(ncores): cpu_batch32_dssim_grad_ms(ncores)}
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         n_cpu = 64
@@ -425,6 +445,14 @@ def side_benchmarks(pkg, dev):
         out[f"batch64_3x512x512_{tag}_ssim_grad_ms"] = ms
         out[f"batch64_3x512x512_{tag}_ssim_grad_hbm_frac"] = x.numel() * (2 * nb + 4) / (ms / 1e3) / 1e9 / measured_peaks()[0]
         del x, y, g
+    # Float64 inputs, values and gradient (the double-precision kernel): 16 x 3 x 512 x 512
+    x, y = syn.device_pair((3, 512, 512, 16), 0.1, dtype=torch.float64, device=dev)
+    s = torch.empty(16, dtype=torch.float64, device=dev)
+    g = pkg.jl_empty((3, 512, 512, 16), torch.float64, dev)
+    ms = timed(lambda: pkg.ssim_with_gradient_(s, g, x, y, None, True), reps=5)
+    out["batch16_3x512x512_f64_ssim_grad_ms"] = ms
+    out["batch16_3x512x512_f64_ssim_grad_gelem_s"] = x.numel() / (ms / 1e3) / 1e9
+    del x, y, g
     # one autograd step (values, then the pullback of a per-image cotangent) on 64 x 3 x 512 x 512:
     # the reference's rrule (gradient with the values, broadcast in the pullback) against the
     # deferred rule (values only, then one gradient launch with the cotangent folded in)
@@ -449,7 +477,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
-    ap.add_argument("--profile-case", choices=["fused", "fwd", "fused_u8", "fused_f16", "fhd1", "fhd3"],
+    ap.add_argument("--profile-case", choices=["fused", "fwd", "fused_u8", "fused_f16", "fused_f64", "fhd1", "fhd3"],
                     default=None,
                     help="only run one kernel on a small case (a size for ncu captures): "
                          "warmup + steps launches and their mean time")
@@ -471,10 +499,14 @@ def profile_case(args):
     pkg = ge.load_package()
     syn = __import__(pkg.__name__ + ".synthetic", fromlist=["x"])
     shape = {"fhd1": (1, 1080, 1920, 1), "fhd3": (3, 1080, 1920, 1)}.get(args.profile_case, (C, H, W, 64))
-    dt = {"fused_u8": torch.uint8, "fused_f16": torch.float16}.get(args.profile_case, torch.float32)
+    dt = {"fused_u8": torch.uint8, "fused_f16": torch.float16,
+          "fused_f64": torch.float64}.get(args.profile_case, torch.float32)
+    if args.profile_case == "fused_f64":   # Float64 inputs, values and gradient (16 images)
+        shape = (C, H, W, 16)
+    odt = torch.float64 if dt == torch.float64 else torch.float32
     x, y = syn.device_pair(shape, NOISE, dtype=dt)
-    s = torch.empty(shape[3], dtype=torch.float32, device="cuda")
-    g = pkg.jl_empty(shape, torch.float32)
+    s = torch.empty(shape[3], dtype=odt, device="cuda")
+    g = pkg.jl_empty(shape, odt)
     def launch():
         if args.profile_case.startswith("fused"):
             pkg.ssim_with_gradient_(s, g, x, y, None, True)
