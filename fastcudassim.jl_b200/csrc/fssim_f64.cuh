@@ -100,20 +100,37 @@ __global__ void __launch_bounds__(D64Geo::NT, 2) f64_kernel(const Params p)
 #define FSSIM_KD(tap) k[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
     const double C1 = p.C1, C2 = p.C2;
 
-    // ---- phase 1: input tile, rows h0-2R .., columns w0-2R ..; zero outside the image
-    for (int e = tid; e < TI * TI; e += NT) {
-        const int r = e % TI, q = e / TI;
-        const int hr = h0 - 2 * RAD + r, wc = w0 - 2 * RAD + q;
-        double xv = 0.0, yv = 0.0;
-        if (hr >= 0 && hr < H && wc >= 0 && wc < W) {
+    // ---- phase 1: input tile, rows h0-2R .., columns w0-2R ..; zero outside the image.
+    // Every load of a thread is issued before the first store, so their latencies overlap.
+    const bool f64in = p.xdt == DT_F64 && p.ydt == DT_F64;
+    {
+        constexpr int NL = (TI * TI + NT - 1) / NT;
+        double xv[NL], yv[NL];
+#pragma unroll
+        for (int u = 0; u < NL; ++u) {
+            const int e = tid + u * NT;
+            const int r = e % TI, q = e / TI;
+            const int hr = h0 - 2 * RAD + r, wc = w0 - 2 * RAD + q;
             const int64_t g = ibase + static_cast<int64_t>(C) * hr + CH * wc;
-            if (FSSIM_IN_BOUNDS(g, p.total_elems, SITE_F64_LOAD)) {
-                xv = ld_f64(p.x, p.xdt, g);
-                yv = ld_f64(p.y, p.ydt, g);
+            const bool ok = e < TI * TI && hr >= 0 && hr < H && wc >= 0 && wc < W &&
+                            FSSIM_IN_BOUNDS(g, p.total_elems, SITE_F64_LOAD);
+            if (f64in) {
+                xv[u] = ok ? __ldg(reinterpret_cast<const double*>(p.x) + g) : 0.0;
+                yv[u] = ok ? __ldg(reinterpret_cast<const double*>(p.y) + g) : 0.0;
+            } else {
+                xv[u] = ok ? ld_f64(p.x, p.xdt, g) : 0.0;
+                yv[u] = ok ? ld_f64(p.y, p.ydt, g) : 0.0;
             }
         }
-        xs[r * XS + q] = xv;
-        ys[r * XS + q] = yv;
+#pragma unroll
+        for (int u = 0; u < NL; ++u) {
+            const int e = tid + u * NT;
+            if (e < TI * TI) {
+                const int r = e % TI, q = e / TI;
+                xs[r * XS + q] = xv[u];
+                ys[r * XS + q] = yv[u];
+            }
+        }
     }
     __syncthreads();
     // ---- phase 2: h-direction pass; item = (moment pair, row group, column)
@@ -238,6 +255,21 @@ __global__ void __launch_bounds__(D64Geo::NT, 2) f64_kernel(const Params p)
         // ---- phase 5: w-direction pass and the combine on the own pixels
         {
             const int r = tid % TO, cg = tid / TO;
+            const int hg = h0 + r;
+            double xo[V4], yo[V4];   // x and y of the own pixels, loaded before the arithmetic
+#pragma unroll
+            for (int o = 0; o < V4; ++o) {
+                const int wg = w0 + cg * V4 + o;
+                const int64_t g = ibase + static_cast<int64_t>(C) * hg + CH * wg;
+                const bool ok = hg < H && wg < W && FSSIM_IN_BOUNDS(g, p.total_elems, SITE_F64_GRAD);
+                if (f64in) {
+                    xo[o] = ok ? __ldg(reinterpret_cast<const double*>(p.x) + g) : 0.0;
+                    yo[o] = ok ? __ldg(reinterpret_cast<const double*>(p.y) + g) : 0.0;
+                } else {
+                    xo[o] = ok ? ld_f64(p.x, p.xdt, g) : 0.0;
+                    yo[o] = ok ? ld_f64(p.y, p.ydt, g) : 0.0;
+                }
+            }
             double a[3][V4];
 #pragma unroll
             for (int j = 0; j < 3; ++j)
@@ -255,16 +287,14 @@ __global__ void __launch_bounds__(D64Geo::NT, 2) f64_kernel(const Params p)
                     }
                 }
             }
-            const int hg = h0 + r;
 #pragma unroll
             for (int o = 0; o < V4; ++o) {
                 const int wg = w0 + cg * V4 + o;
                 if (hg < H && wg < W) {
                     const int64_t g = ibase + static_cast<int64_t>(C) * hg + CH * wg;
                     if (FSSIM_IN_BOUNDS(g, p.total_elems, SITE_F64_GRAD)) {
-                        const double xv = ld_f64(p.x, p.xdt, g), yv = ld_f64(p.y, p.ydt, g);
                         // src/core.jl:773-782: 2 x K(dQ) + K(dM) + y K(dP), 2 dQ stored doubled
-                        const double gv = fma(xv, a[0][o], fma(yv, a[2][o], a[1][o]));
+                        const double gv = fma(xo[o], a[0][o], fma(yo[o], a[2][o], a[1][o]));
                         if (p.gdt == DT_F64) reinterpret_cast<double*>(p.grad)[g] = gv;
                         else st_grad(p.grad, p.gdt, g, static_cast<float>(gv));
                     }
