@@ -83,13 +83,13 @@ __global__ void __launch_bounds__(D64Geo::NT, 2) f64_kernel(const Params p)
     double* red = reinterpret_cast<double*>(smem_raw + G::in_bytes + G::h1_bytes);
 
     const int tid = threadIdx.x;
-    int64_t blk = blockIdx.x;
-    const int c = static_cast<int>(blk % p.C);
-    blk /= p.C;
-    const int tw = static_cast<int>(blk % p.nseg);   // tile column
-    blk /= p.nseg;
-    const int th = static_cast<int>(blk % p.nb);     // tile row
-    const int n = static_cast<int>(blk / p.nb);
+    // block -> (channel, tile column, tile row, image); 32-bit divisions (grid < 2^31)
+    const uint32_t b0 = blockIdx.x, b1q = b0 / static_cast<uint32_t>(p.C);
+    const uint32_t b2q = b1q / static_cast<uint32_t>(p.nseg), b3q = b2q / static_cast<uint32_t>(p.nb);
+    const int c = static_cast<int>(b0 - b1q * static_cast<uint32_t>(p.C));
+    const int tw = static_cast<int>(b1q - b2q * static_cast<uint32_t>(p.nseg));   // tile column
+    const int th = static_cast<int>(b2q - b3q * static_cast<uint32_t>(p.nb));     // tile row
+    const int n = static_cast<int>(b3q);
     const int C = p.C, H = p.H, W = p.W;
     const int64_t CH = static_cast<int64_t>(C) * H;
     const int64_t ibase = static_cast<int64_t>(n) * p.img_elems + c;

@@ -513,21 +513,24 @@ __global__ void __launch_bounds__(TGeo::NT, 3) tile_fwd_kernel(const Params p)
         int n, th, tw, c;
         int64_t ibase;
     };
-    auto tile_of = [&](int64_t t) {
+    // tile index -> (channel, tile column, tile row, image); 32-bit divisions, as the
+    // host keeps the tile count below 2^31
+    auto tile_of = [&](int64_t t64) {
         Tile u;
-        u.c = static_cast<int>(t % C);
-        t /= C;
-        u.tw = static_cast<int>(t % p.nseg);
-        t /= p.nseg;
-        u.th = static_cast<int>(t % p.nb);
-        u.n = static_cast<int>(t / p.nb);
+        uint32_t t = static_cast<uint32_t>(t64);
+        const uint32_t tc = t / static_cast<uint32_t>(C);
+        u.c = static_cast<int>(t - tc * static_cast<uint32_t>(C));
+        const uint32_t ts = tc / static_cast<uint32_t>(p.nseg);
+        u.tw = static_cast<int>(tc - ts * static_cast<uint32_t>(p.nseg));
+        const uint32_t tb = ts / static_cast<uint32_t>(p.nb);
+        u.th = static_cast<int>(ts - tb * static_cast<uint32_t>(p.nb));
+        u.n = static_cast<int>(tb);
         u.ibase = static_cast<int64_t>(u.n) * p.img_elems + u.c;
         return u;
     };
     // element e of a tile <-> stage row r = e % IR, column q = e / IR; zero outside the image;
     // all loads of the tile are issued before the first conversion
-    auto load_convert = [&](int64_t t, float2* buf) {
-        const Tile u = tile_of(t);
+    auto load_convert = [&](const Tile& u, float2* buf) {
         uint32_t rx[G::NL], ry[G::NL];
 #pragma unroll
         for (int k = 0; k < G::NL; ++k) {
@@ -566,9 +569,9 @@ __global__ void __launch_bounds__(TGeo::NT, 3) tile_fwd_kernel(const Params p)
 #pragma unroll 1
     for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
         float2* st = stage;
-        load_convert(t, st);
-        __syncthreads();   // the stage is complete; the previous tile's F2 is done with f1
         const Tile u = tile_of(t);
+        load_convert(u, st);
+        __syncthreads();   // the stage is complete; the previous tile's F2 is done with f1
 
         // ---- F1: rows V*q1 .. V*q1+V-1 of column q (stage rows V*q1 .. V*q1+V+2R-1)
         {
