@@ -110,6 +110,22 @@ enum BoundsSite : unsigned {
     SITE_FPIPE_STAGE, SITE_FPIPE_RAW
 };
 
+// Block index -> (channel, width segment, band, image) of the streaming kernels, whose
+// grid is ordered channel fastest.  32-bit divisions: the host keeps grids below 2^31.
+struct BandIndex {
+    int c, seg, band, n;
+};
+__device__ __forceinline__ BandIndex band_index(const Params& p)
+{
+    const uint32_t b0 = blockIdx.x;
+    const uint32_t q1 = b0 / static_cast<uint32_t>(p.C);
+    const uint32_t q2 = q1 / static_cast<uint32_t>(p.nseg);
+    const uint32_t q3 = q2 / static_cast<uint32_t>(p.nb);
+    return BandIndex{static_cast<int>(b0 - q1 * static_cast<uint32_t>(p.C)),
+                     static_cast<int>(q1 - q2 * static_cast<uint32_t>(p.nseg)),
+                     static_cast<int>(q2 - q3 * static_cast<uint32_t>(p.nb)), static_cast<int>(q3)};
+}
+
 // Raw bits of one input element (zero-extended); converted at staging time so
 // that the load's latency is not exposed at the point of issue.
 __device__ __forceinline__ uint32_t ld_raw(const void* base, int dt, int64_t idx)

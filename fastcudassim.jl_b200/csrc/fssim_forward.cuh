@@ -47,13 +47,8 @@ __global__ void __launch_bounds__(NT, 512 / NT) band_kernel(const Params p)
     double* red = reinterpret_cast<double*>(smem_raw + G::total - G::red_bytes);
 
     const int tid = threadIdx.x;
-    int64_t blk = blockIdx.x;
-    const int c = static_cast<int>(blk % p.C);
-    blk /= p.C;
-    const int seg = static_cast<int>(blk % p.nseg);
-    blk /= p.nseg;
-    const int band = static_cast<int>(blk % p.nb);
-    const int n = static_cast<int>(blk / p.nb);
+    const BandIndex bi = band_index(p);
+    const int c = bi.c, seg = bi.seg, band = bi.band, n = bi.n;
     const int C = p.C, H = p.H, W = p.W;
     const int64_t CH = static_cast<int64_t>(C) * H;   // element stride of one column
     const int h0 = band * T;
@@ -253,13 +248,8 @@ __global__ void __launch_bounds__(2 * NT, 512 / (2 * NT)) fwd_pipe_kernel(const 
     double* red = reinterpret_cast<double*>(smem_raw + G::off_red);
 
     const int tid = threadIdx.x;
-    int64_t blk = blockIdx.x;
-    const int c = static_cast<int>(blk % p.C);
-    blk /= p.C;
-    const int seg = static_cast<int>(blk % p.nseg);
-    blk /= p.nseg;
-    const int band = static_cast<int>(blk % p.nb);
-    const int n = static_cast<int>(blk / p.nb);
+    const BandIndex bi = band_index(p);
+    const int c = bi.c, seg = bi.seg, band = bi.band, n = bi.n;
     const int C = p.C, H = p.H, W = p.W;
     const int h0 = band * T;
     const int w0 = seg * p.L;
