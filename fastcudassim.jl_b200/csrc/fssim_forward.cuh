@@ -470,7 +470,6 @@ struct TGeo {
     static constexpr int NG = (TW + V - 1) / V;      // F2 column groups of V outputs per row
     static constexpr int FS = NG * V + 2 * RAD + 1;  // F1 row stride (float4), odd, covers the last group
     static constexpr int NE = IR * IC;               // staged elements
-    static constexpr int NL = (NE + NT - 1) / NT;    // staged elements per thread
     static constexpr int stage_one = IC * RS * 8;
     static constexpr int f1_bytes = TH * FS * 16;
     static constexpr int red_bytes = (NT / 32 + 2) * 8;
@@ -518,33 +517,48 @@ __global__ void __launch_bounds__(TGeo::NT, 3) tile_fwd_kernel(const Params p)
         u.ibase = static_cast<int64_t>(u.n) * p.img_elems + u.c;
         return u;
     };
-    // element e of a tile <-> stage row r = e % IR, column q = e / IR; zero outside the image;
-    // all loads of the tile are issued before the first conversion
+    // Stage element (row r, column q) of a tile.  Thread tid < LG * IR loads row
+    // r = tid % IR of columns q = tid / IR + LG j (a warp reads consecutive rows of a
+    // column), so its row test is made once and each column costs one test and one
+    // pointer step; zero outside the image.  All loads of the tile are issued before the
+    // first store.
+    constexpr int LG = G::NT / IR;                 // column phases
+    constexpr int NJ = (IC + LG - 1) / LG;         // columns per thread
     auto load_convert = [&](const Tile& u, float2* buf) {
-        uint32_t rx[G::NL], ry[G::NL];
+        const int r = tid % IR, q0 = tid / IR;
+        const int hr = u.th * TH - RAD + r, wc0 = u.tw * TW - RAD + q0;
+        const bool row_ok = tid < LG * IR && hr >= 0 && hr < H;
+        // element index of (row r, column q0); a masked load never uses it
+        const int64_t g0 = u.ibase + static_cast<int64_t>(C) * hr + CH * wc0;
+        const int64_t gstep = CH * LG;
+        uint32_t rx[NJ], ry[NJ];
+        const unsigned int* px = reinterpret_cast<const unsigned int*>(p.x) + g0;
+        const unsigned int* py = reinterpret_cast<const unsigned int*>(p.y) + g0;
 #pragma unroll
-        for (int k = 0; k < G::NL; ++k) {
-            const int e = tid + G::NT * k;
-            const int r = e % IR, q = e / IR;
-            const int hr = u.th * TH - RAD + r, wc = u.tw * TW - RAD + q;
-            bool ok = e < G::NE && hr >= 0 && hr < H && wc >= 0 && wc < W;
-            const int64_t g = u.ibase + static_cast<int64_t>(C) * (ok ? hr : 0) + CH * (ok ? wc : 0);
-            ok = ok && FSSIM_IN_BOUNDS(g, p.total_elems, SITE_TILE_LOAD);
+        for (int j = 0; j < NJ; ++j) {
+            const int wc = wc0 + LG * j;
+            const int64_t g = g0 + gstep * j;
+            const bool ok = row_ok && (j < NJ - 1 || q0 + LG * j < IC) &&
+                            static_cast<unsigned>(wc) < static_cast<unsigned>(W) &&
+                            FSSIM_IN_BOUNDS(g, p.total_elems, SITE_TILE_LOAD);
             if (IM == 0) {
-                rx[k] = ok ? __ldg(reinterpret_cast<const unsigned int*>(p.x) + g) : 0u;
-                ry[k] = ok ? __ldg(reinterpret_cast<const unsigned int*>(p.y) + g) : 0u;
+                rx[j] = ok ? __ldg(px) : 0u;
+                ry[j] = ok ? __ldg(py) : 0u;
+                px += gstep;
+                py += gstep;
             } else {
-                rx[k] = ok ? ld_in<IM>(p.x, p.xdt, g) : 0u;
-                ry[k] = ok ? ld_in<IM>(p.y, p.ydt, g) : 0u;
+                rx[j] = ok ? ld_in<IM>(p.x, p.xdt, g) : 0u;
+                ry[j] = ok ? ld_in<IM>(p.y, p.ydt, g) : 0u;
             }
         }
+        if (tid < LG * IR) {
+            float2* d = buf + q0 * RS + r;
 #pragma unroll
-        for (int k = 0; k < G::NL; ++k) {
-            const int e = tid + G::NT * k;
-            if (e < G::NE)
-                buf[(e / IR) * RS + e % IR] =
-                    IM == 0 ? make_float2(__uint_as_float(rx[k]), __uint_as_float(ry[k]))
-                            : make_float2(cvt_in<IM>(rx[k], p.xdt), cvt_in<IM>(ry[k], p.ydt));
+            for (int j = 0; j < NJ; ++j) {
+                if (j < NJ - 1 || q0 + LG * j < IC)
+                    d[LG * j * RS] = IM == 0 ? make_float2(__uint_as_float(rx[j]), __uint_as_float(ry[j]))
+                                             : make_float2(cvt_in<IM>(rx[j], p.xdt), cvt_in<IM>(ry[j], p.ydt));
+            }
         }
     };
 
