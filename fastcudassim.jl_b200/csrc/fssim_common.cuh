@@ -47,6 +47,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <type_traits>
+
 namespace fssim {
 
 constexpr int RAD = 5;              // Gaussian radius (src/core.jl:41)
@@ -204,6 +206,27 @@ __device__ __forceinline__ void cp_async4(void* smem_dst, const void* gsrc, bool
     const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem_dst));
     const int sz = valid ? 4 : 0;
     asm volatile("cp.async.ca.shared.global [%0], [%1], 4, %2;\n" ::"r"(s), "l"(gsrc), "r"(sz) : "memory");
+}
+// The same copy at a compile-time byte offset from a shared-memory address, with an
+// explicit source size (4, or 0 to zero-fill without reading the source).
+template <int DOFF>
+__device__ __forceinline__ void cp_async4_at(unsigned sdst, const void* gsrc, int sz)
+{
+    asm volatile("cp.async.ca.shared.global [%0+%3], [%1], 4, %2;\n" ::"r"(sdst), "l"(gsrc), "r"(sz), "n"(DOFF)
+                 : "memory");
+}
+__device__ __forceinline__ unsigned smem_addr(const void* p)
+{
+    return static_cast<unsigned>(__cvta_generic_to_shared(p));
+}
+// f(std::integral_constant<int, I>) for I = B..E-1, where an offset must be a constant.
+template <int B, int E, class F>
+__device__ __forceinline__ void static_for(F&& f)
+{
+    if constexpr (B < E) {
+        f(std::integral_constant<int, B>{});
+        static_for<B + 1, E>(f);
+    }
 }
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>

@@ -285,24 +285,47 @@ __global__ void __launch_bounds__(2 * NT, 512 / (2 * NT)) fwd_pipe_kernel(const 
             lrow_ok[r] = i < R2 && hr >= 0 && hr < H;
             lrow_off[r] = static_cast<uint32_t>(C) * static_cast<uint32_t>(lrow_ok[r] ? hr : 0);
         }
+        // Float32 stage copies: thread ta copies row ta (and row ta + NT while that is below
+        // R2) of each column of the step.  The row sizes are per-thread constants (4, or 0
+        // outside the image: a zero-size copy fills zeros and does not read its source, so a
+        // masked row's address may lie outside the image); a column costs one address per input.
+        static_assert(G::LROWS <= 2 && R2 - NT <= NT, "at most one extra stage row per thread");
+        const int rsz0 = lrow_ok[0] ? 4 : 0;
+        const int rsz1 = G::LROWS > 1 && lrow_ok[G::LROWS - 1] ? 4 : 0;
+        const float* xr0 = xg + static_cast<int64_t>(C) * (h0 - LAG + ta);
+        const float* yr0 = yg + static_cast<int64_t>(C) * (h0 - LAG + ta);
+        const float* xr1 = xr0 + static_cast<int64_t>(C) * NT;
+        const float* yr1 = yr0 + static_cast<int64_t>(C) * NT;
         auto issue_stage = [&](int k, float2* buf) {   // stage <- input columns of step k
             const int cb = w0 - LAG + k * S;
-#pragma unroll
-            for (int j = 0; j < S; ++j) {
+            const unsigned sd = smem_addr(buf + ta * SP);
+            static_for<0, S>([&](auto jj) {
+                constexpr int j = decltype(jj)::value;
                 const int wc = cb + j;
                 const bool colok = static_cast<unsigned>(wc) < static_cast<unsigned>(W);
-                const uint32_t coloff = CH32 * static_cast<uint32_t>(colok ? wc : 0);
-#pragma unroll
-                for (int r = 0; r < G::LROWS; ++r) {
-                    const int i = ta + NT * r;
-                    if (G::LROWS == 1 || i < R2) {
-                        const uint32_t off = lrow_off[r] + coloff;
-                        const bool ok = lrow_ok[r] && colok &&
-                                        FSSIM_IN_BOUNDS(ibase + off, p.total_elems, SITE_FPIPE_STAGE);
-                        cp_async4(&buf[i * SP + j].x, xg + off, ok);
-                        cp_async4(&buf[i * SP + j].y, yg + off, ok);
-                    }
-                }
+                const uint32_t coff = CH32 * static_cast<uint32_t>(colok ? wc : 0);
+                int sz = colok ? rsz0 : 0;
+#ifdef FSSIM_DEBUG_BOUNDS
+                if (sz && !FSSIM_IN_BOUNDS(ibase + lrow_off[0] + coff, p.total_elems, SITE_FPIPE_STAGE)) sz = 0;
+#endif
+                cp_async4_at<j * 8>(sd, xr0 + coff, sz);
+                cp_async4_at<j * 8 + 4>(sd, yr0 + coff, sz);
+            });
+            if (G::LROWS > 1 && ta < R2 - NT) {
+                static_for<0, S>([&](auto jj) {
+                    constexpr int j = decltype(jj)::value;
+                    const int wc = cb + j;
+                    const bool colok = static_cast<unsigned>(wc) < static_cast<unsigned>(W);
+                    const uint32_t coff = CH32 * static_cast<uint32_t>(colok ? wc : 0);
+                    int sz = colok ? rsz1 : 0;
+#ifdef FSSIM_DEBUG_BOUNDS
+                    if (sz && !FSSIM_IN_BOUNDS(ibase + lrow_off[G::LROWS - 1] + coff, p.total_elems,
+                                               SITE_FPIPE_STAGE))
+                        sz = 0;
+#endif
+                    cp_async4_at<NT * SP * 8 + j * 8>(sd, xr1 + coff, sz);
+                    cp_async4_at<NT * SP * 8 + j * 8 + 4>(sd, yr1 + coff, sz);
+                });
             }
         };
         // converting loader: raw bits of step k in registers, stored converted by store_raw
