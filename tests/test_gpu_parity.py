@@ -204,6 +204,33 @@ def test_float64_inputs_compute_in_double(pkg, orc, xdt, ydt, shape):
         assert np.max(np.abs(fv.cpu().numpy() - rv)) <= 1e-10
 
 
+@pytest.mark.parametrize("shape", [(3, 65, 33, 3), (1, 32, 97, 2)])
+def test_float64_gradient_only_and_narrow_gradient_outputs(pkg, orc, shape):
+    """Float64 inputs through the gradient-only entry points (no values computed), into
+    Float64, Float32 and Float16 gradient buffers; tiles with one row or one column
+    inside the image sit on the right and bottom edges."""
+    syn = _syn(pkg)
+    x, y = syn.host_pair(67, shape, 0.1, dtype=np.float64)
+    xt, yt = pkg.jl_from_numpy(x), pkg.jl_from_numpy(y)
+    for dssim in (False, True):
+        _, rg = orc.ssim(x, y, flags=orc.USE_DSSIM if dssim else 0, precision="f64")
+        g = pkg.dssim_gradient(xt, yt) if dssim else pkg.ssim_gradient(xt, yt)
+        assert g.dtype == torch.float64
+        assert _rel_l2(pkg.jl_to_numpy(g), rg) <= 1e-9
+        # computed in double and rounded once: within one unit in the last place of the
+        # oracle's value rounded to the buffer's dtype (Float16 values here are subnormal)
+        for gdt, npdt in ((torch.float32, np.float32), (torch.float16, np.float16)):
+            gb = pkg.jl_empty(shape, gdt)
+            if dssim:
+                pkg.dssim_gradient_(gb, xt, yt, None)
+            else:
+                pkg.ssim_gradient_(gb, xt, yt, None)
+            want = rg.astype(npdt)
+            ulp = np.spacing(np.abs(want)).astype(np.float64)
+            err = np.abs(pkg.jl_to_numpy(gb).astype(np.float64) - want.astype(np.float64))
+            assert np.all(err <= ulp), (gdt, float(np.max(err / ulp)))
+
+
 def test_float64_gradient_output_from_float32_inputs(pkg, orc):
     x, y = _syn(pkg).host_pair(62, (3, 64, 48, 2), 0.1)
     xt, yt = pkg.jl_from_numpy(x), pkg.jl_from_numpy(y)
