@@ -508,7 +508,7 @@ struct TGeo {
 // smaller than the tile count.  A resident CTA's next tile streaming in behind
 // the current one was measured slower: it halves the CTAs per SM.
 template <int IM>
-__global__ void __launch_bounds__(TGeo::NT, 3) tile_fwd_kernel(const Params p)
+__global__ void __launch_bounds__(TGeo::NT, 4) tile_fwd_kernel(const Params p)
 {
     using G = TGeo;
     constexpr int TH = G::TH, TW = G::TW, IR = G::IR, IC = G::IC, RS = G::RS, FS = G::FS;
