@@ -137,18 +137,18 @@ __device__ __forceinline__ uint32_t ld_raw(const void* base, int dt, int64_t idx
     return __ldg(reinterpret_cast<const unsigned char*>(base) + idx);
 }
 
-// N0f8 -> Float32: the correctly rounded value of raw/255.  q = raw * fl(1/255)
-// is off by one ulp for about half of the 256 bytes; one Newton correction step
-// for a constant divisor (residual e = raw - 255 q by FMA, then q + e * fl(1/255))
-// gives the correctly rounded quotient for every byte (checked exhaustively, and
-// against the division by a GPU test).
+// N0f8 -> Float32: the correctly rounded value of raw/255.  1/255 is split into
+// hi = fl(1/255) and lo = fl(1/255 - hi); fma(raw, hi, raw * lo) is within about
+// 2^-47 (relative) of raw/255 before its single rounding, while raw/255 lies at
+// least about 2^-32 (relative) from every rounding boundary, so the result is the
+// correctly rounded quotient for every byte (checked exhaustively in exact rational
+// arithmetic).  raw * fl(1/255) alone is off by one ulp for about half the bytes.
 __device__ __forceinline__ float n0f8_to_f32(uint32_t r)
 {
-    const float inv = 1.0f / 255.0f;
+    const float hi = __uint_as_float(0x3b808081u);   // fl(1/255)
+    const float lo = __uint_as_float(0xaf7efeffu);   // fl(1/255 - fl(1/255))
     const float fr = static_cast<float>(r & 255u);
-    const float q = fr * inv;
-    const float e = fmaf(-q, 255.0f, fr);
-    return fmaf(e, inv, q);
+    return fmaf(fr, hi, fr * lo);
 }
 
 __device__ __forceinline__ float cvt_raw(uint32_t r, int dt, const float* /*unused*/)

@@ -83,9 +83,10 @@ def test_synthetic_generator_is_reproducible(pkg):
 
 
 def test_n0f8_conversion_formula_is_correctly_rounded():
-    """The kernels convert N0f8 with q = r*fl(1/255) and one FMA correction
-    (q + fma(-q, 255, r) * fl(1/255)); exact rational arithmetic shows it equals
-    the correctly rounded r/255 for all 256 bytes (FixedPointNumbers' value)."""
+    """The kernels convert N0f8 as fma(r, hi, r * lo) with hi = fl(1/255) and
+    lo = fl(1/255 - hi) (the bit patterns in n0f8_to_f32); exact rational arithmetic
+    shows it equals the correctly rounded r/255 for all 256 bytes (FixedPointNumbers'
+    value), while r * fl(1/255) alone does not."""
     from fractions import Fraction
 
     def rne32(q: Fraction) -> np.float32:
@@ -93,9 +94,14 @@ def test_n0f8_conversion_formula_is_correctly_rounded():
         cands = [np.nextafter(c, np.float32(-1)), c, np.nextafter(c, np.float32(2))]
         return min(cands, key=lambda v: (abs(Fraction(float(v)) - q), int(np.array(v).view(np.uint32)) & 1))
 
-    inv = np.float32(1.0) / np.float32(255.0)
+    hi = np.array(0x3B808081, np.uint32).view(np.float32)
+    lo = np.array(0xAF7EFEFF, np.uint32).view(np.float32)
+    assert hi == rne32(Fraction(1, 255)) and lo == rne32(Fraction(1, 255) - Fraction(float(hi)))
+    plain_off = 0
     for r in range(256):
-        q = np.float32(np.float32(r) * inv)
-        e = rne32(Fraction(float(-q)) * 255 + r)
-        got = rne32(Fraction(float(e)) * Fraction(float(inv)) + Fraction(float(q)))
-        assert got == rne32(Fraction(r, 255)), r
+        p = rne32(Fraction(r) * Fraction(float(lo)))                          # r * lo
+        got = rne32(Fraction(r) * Fraction(float(hi)) + Fraction(float(p)))   # one rounding (FMA)
+        want = rne32(Fraction(r, 255))
+        assert got == want, r
+        plain_off += rne32(Fraction(r) * Fraction(float(hi))) != want
+    assert plain_off > 0
