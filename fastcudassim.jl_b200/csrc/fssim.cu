@@ -75,19 +75,20 @@ KInfo kinfo()
                  fssim::Geo<NT>::S, NT};
 }
 
-// Forward two-group pipeline (Float32, images below 2^31 elements).
-template <int NT>
+// Forward two-group pipeline (images below 2^31 elements); IOM as pipe_kernel.
+template <int NT, int IOM>
 KInfo fpinfo()
 {
-    return KInfo{reinterpret_cast<const void*>(&fssim::fwd_pipe_kernel<NT>), fssim::FPGeo<NT>::total, NT,
+    return KInfo{reinterpret_cast<const void*>(&fssim::fwd_pipe_kernel<NT, IOM>), fssim::FPGeo<NT>::total, NT,
                  fssim::FPGeo<NT>::S, 2 * NT};
 }
 
+template <int IOM>
 KInfo fpinfo_nt(int nt)
 {
-    if (nt == 64) return fpinfo<64>();
-    if (nt == 96) return fpinfo<96>();
-    return fpinfo<128>();
+    if (nt == 64) return fpinfo<64, IOM>();
+    if (nt == 96) return fpinfo<96, IOM>();
+    return fpinfo<128, IOM>();
 }
 
 template <int NT, bool WS, int IOM>
@@ -119,21 +120,18 @@ KInfo tile_info(bool f32io, int iom)
     return tinfo<fssim::IN_ANY>();
 }
 
-// Forward-only routing, from B200 measurements of both kernels on batches and on
-// single images.  Converted inputs (N0f8, Float16, mixed) always run on the tile
-// kernel: it was faster for N0f8 at every size (9-13%) and for Float16 equal or
-// faster.  Float32 calls up to 4 Mi elements run on tiles too (a streaming grid
-// would need many short segments), and so does one multi-channel image up to
-// 8 Mi elements (3 x 1080 x 1920: 44 vs 47 us); larger Float32 calls stream
-// (fwd_pipe_kernel: 271 vs 387 us on 64 x 3 x 512 x 512).
+// Forward-only calls up to 4 Mi elements run on the tile kernel: a streaming
+// grid would need many short segments (halo warm-up, few warps per CTA).
+// Larger calls stream (fwd_pipe_kernel), except mixed input dtypes (decoded
+// per element, the streaming loader would spill) and converted inputs in
+// images of 2^31 elements or more, which only the tile kernel reads with
+// 64-bit offsets.
 constexpr int64_t kTileMaxElems = int64_t(1) << 22;
-constexpr int64_t kTileMaxElemsOneImage = int64_t(1) << 23;
 
-bool use_tiles(int64_t c, int64_t h, int64_t w, int64_t n, bool f32io, int /*iom*/)
+bool use_tiles(int64_t c, int64_t h, int64_t w, int64_t n, bool f32io, int iom)
 {
-    if (!f32io) return true;
-    const int64_t elems = c * h * w * n;
-    return elems <= kTileMaxElems || (n == 1 && c >= 3 && elems <= kTileMaxElemsOneImage);
+    if (c * h * w * n <= kTileMaxElems) return true;
+    return !f32io && (iom == fssim::IN_ANY || c * h * w >= (int64_t(1) << 31));
 }
 
 template <bool F, bool WS>
@@ -157,7 +155,10 @@ KInfo kernel_info(int nt, bool fused, bool want_ssim, bool f32io, int iom, bool 
             default: return pinfo_io<fssim::IN_ANY>(nt, want_ssim);
         }
     }
-    if (small_image) return fpinfo_nt(nt);   // Float32 (other input dtypes run as tiles, see use_tiles)
+    if (small_image) {   // 32-bit in-image offsets; mixed dtypes run as tiles (see use_tiles)
+        if (f32io) return fpinfo_nt<0>(nt);
+        return iom == fssim::IN_U8 ? fpinfo_nt<fssim::IN_U8>(nt) : fpinfo_nt<fssim::IN_F16>(nt);
+    }
     // images of 2^31 elements or more: Float32 only (converted inputs run as tiles)
     if (nt == 64) return kinfo<64>();
     if (nt == 96) return kinfo<96>();

@@ -109,7 +109,7 @@ __device__ __forceinline__ bool in_bounds(int64_t idx, int64_t limit, unsigned s
 enum BoundsSite : unsigned {
     SITE_BAND_LOAD = 1, SITE_PIPE_STAGE, SITE_PIPE_XY, SITE_PIPE_STAGE_RAW, SITE_PIPE_XY_RAW,
     SITE_PIPE_GRAD, SITE_TILE_LOAD, SITE_F64_LOAD, SITE_F64_GRAD, SITE_PARTIALS, SITE_COUNTERS,
-    SITE_FPIPE_STAGE
+    SITE_FPIPE_STAGE, SITE_FPIPE_RAW
 };
 
 // Block index -> (channel, width segment, band, image) of the streaming kernels, whose

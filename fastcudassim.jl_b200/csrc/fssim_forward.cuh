@@ -211,10 +211,10 @@ __global__ void __launch_bounds__(NT, 512 / NT) band_kernel(const Params p)
 // pipe_kernel.  Group A loads step t+1 and runs F1(t); group B runs F2(t-1)
 // and the SSIM map.  One barrier per slot; the F1 output and the staging tile
 // are double-buffered by slot parity; group B keeps the F1 history of its row
-// as two 8-column blocks used in turn.  Float32 inputs through cp.async (other
-// input dtypes run as tiles, which measured faster for them at every size).
-// In-image offsets are 32-bit (the host routes images of 2^31 elements or more
-// elsewhere).
+// as two 8-column blocks used in turn.  IOM 0: Float32 inputs through
+// cp.async; otherwise (an InMode) group A loads raw elements into registers a
+// slot ahead and converts them when it stores them.  In-image offsets are
+// 32-bit (the host routes images of 2^31 elements or more elsewhere).
 // ---------------------------------------------------------------------------
 template <int NT>
 struct FPGeo {
@@ -233,9 +233,10 @@ struct FPGeo {
     static_assert(stage_one % 16 == 0 && f1_one % 16 == 0, "16-byte alignment of the buffers");
 };
 
-template <int NT>
+template <int NT, int IOM>
 __global__ void __launch_bounds__(2 * NT, 512 / (2 * NT)) fwd_pipe_kernel(const Params p)
 {
+    constexpr bool F32IO = IOM == 0;
     using G = FPGeo<NT>;
     constexpr int S = G::S, R1 = G::R1, T = G::T, R2 = G::R2, LAG = G::LAG;
     constexpr int SP = G::SP, FC = G::FC;
@@ -327,14 +328,52 @@ __global__ void __launch_bounds__(2 * NT, 512 / (2 * NT)) fwd_pipe_kernel(const 
                 });
             }
         };
-        issue_stage(0, stage);
-        cp_async_commit();
-        cp_async_wait<0>();
+        // converting loader: raw bits of step k in registers, stored converted by store_raw
+        uint32_t rsx[F32IO ? 1 : G::LROWS * S], rsy[F32IO ? 1 : G::LROWS * S];
+        auto load_raw = [&](int k) {
+            const int cb = w0 - LAG + k * S;
+#pragma unroll
+            for (int j = 0; j < (F32IO ? 0 : S); ++j) {
+                const int wc = cb + j;
+                const bool colok = static_cast<unsigned>(wc) < static_cast<unsigned>(W);
+#pragma unroll
+                for (int r = 0; r < G::LROWS; ++r) {
+                    const int64_t g = ibase + (lrow_off[r] + CH32 * static_cast<uint32_t>(colok ? wc : 0));
+                    const bool ok = lrow_ok[r] && colok && FSSIM_IN_BOUNDS(g, p.total_elems, SITE_FPIPE_RAW);
+                    rsx[r * S + j] = ok ? ld_in<F32IO ? IN_ANY : IOM>(p.x, p.xdt, g) : 0u;
+                    rsy[r * S + j] = ok ? ld_in<F32IO ? IN_ANY : IOM>(p.y, p.ydt, g) : 0u;
+                }
+            }
+        };
+        auto store_raw = [&](float2* buf) {
+#pragma unroll
+            for (int j = 0; j < (F32IO ? 0 : S); ++j) {
+#pragma unroll
+                for (int r = 0; r < G::LROWS; ++r) {
+                    const int i = ta + NT * r;
+                    if (G::LROWS == 1 || i < R2)
+                        buf[i * SP + j] = make_float2(cvt_in<F32IO ? IN_ANY : IOM>(rsx[r * S + j], p.xdt),
+                                                      cvt_in<F32IO ? IN_ANY : IOM>(rsy[r * S + j], p.ydt));
+                }
+            }
+        };
+        if (F32IO) {
+            issue_stage(0, stage);
+            cp_async_commit();
+            cp_async_wait<0>();
+        } else {
+            load_raw(0);
+            store_raw(stage);
+        }
         __syncthreads();
 #pragma unroll 1
         for (int t = 0; t < nslot; ++t) {
-            if (t + 1 < ns) issue_stage(t + 1, stage + ((t + 1) & 1) * STG);
-            cp_async_commit();
+            if (F32IO) {
+                if (t + 1 < ns) issue_stage(t + 1, stage + ((t + 1) & 1) * STG);
+                cp_async_commit();
+            } else if (t + 1 < ns) {
+                load_raw(t + 1);
+            }
             if (t < ns) {   // -------- F1(t): h-direction pass of the 4 moment images --------
                 const float2* st = stage + (t & 1) * STG;
                 float4* f1 = f1buf + (t & 1) * F1N;
@@ -362,7 +401,8 @@ __global__ void __launch_bounds__(2 * NT, 512 / (2 * NT)) fwd_pipe_kernel(const 
                 for (int o = 0; o < V; ++o)
                     f1[(V * q1 + o) * FC + j1] = make_float4(aA[o].x, aA[o].y, aB[o].x, aB[o].y);
             }
-            cp_async_wait<0>();
+            if (F32IO) cp_async_wait<0>();
+            else if (t + 1 < ns) store_raw(stage + ((t + 1) & 1) * STG);
             __syncthreads();
         }
     } else {

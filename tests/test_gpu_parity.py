@@ -240,12 +240,10 @@ def test_float64_gradient_output_from_float32_inputs(pkg, orc):
     assert _rel_l2(pkg.jl_to_numpy(g), rg) <= GRAD_RTOL_L2
 
 
-@pytest.mark.parametrize("shape", [(3, 1100, 1400, 1), (1, 2100, 2100, 1), (1, 600, 800, 10)],
-                         ids=["3x1100x1400", "1x2100x2100", "10x1x600x800"])
+@pytest.mark.parametrize("shape", [(3, 1100, 1400, 1), (1, 600, 800, 10)], ids=["3x1100x1400", "10x1x600x800"])
 def test_forward_streaming_kernel_vs_oracle(pkg, orc, shape):
-    """Float32 forward calls above 4 Mi elements take the streaming kernel, except one image of
-    3 or more channels up to 8 Mi elements (the first case), which runs as tiles; converted inputs
-    always run as tiles.  The same tolerance against the float64 oracle on every path."""
+    """Float32 forward calls above 4 Mi elements take the streaming kernel (smaller ones and
+    converted inputs run as tiles): the same tolerance against the float64 oracle."""
     x, y = _syn(pkg).host_pair(29, shape, 0.1)
     v, _ = _run(pkg, x, y, mode="fwd")
     rv, _ = orc.ssim(x, y, flags=orc.SKIP_BACKWARD, precision="f64")
@@ -296,11 +294,10 @@ def test_forward_on_an_image_of_more_than_2_31_elements(pkg, orc):
     assert abs((float(changed[0]) - float(same[0])) - shift) <= 1e-9 + 1e-4 * abs(shift)
 
 
-@pytest.mark.parametrize("shape", [(3, 1100, 1400, 1), (3, 700, 700, 3)], ids=["3x1100x1400", "3x3x700x700"])
 @pytest.mark.parametrize("dt", ["u8", "f16"])
-def test_forward_converted_inputs_above_4_mi_elements(pkg, orc, dt, shape):
-    """N0f8 and Float16 forward calls run as tiles at every size (converted when the tile is
-    staged), here on one image and on a batch above 4 Mi elements."""
+def test_forward_converted_inputs_on_the_streaming_path(pkg, orc, dt):
+    """N0f8 and Float16 forward calls above 4 Mi elements stream (converted in group A's loader)."""
+    shape = (3, 1100, 1400, 1)
     syn = _syn(pkg)
     if dt == "u8":
         x, y = syn.host_pair(37, shape, 0.1, dtype=np.uint8)
