@@ -126,25 +126,32 @@ def test_input_dtypes_converted_in_kernel(pkg, orc, xdt, ydt):
     assert _rel_l2(g, rg) <= GRAD_RTOL_L2
 
 
+@pytest.mark.parametrize("dt", ["n0f8", "f16"])
 @pytest.mark.parametrize("shape,mode", [((3, 64, 48, 2), "fwd"), ((3, 64, 48, 2), "both"),
                                         ((3, 700, 700, 3), "fwd")], ids=["tiles", "fused", "streaming"])
-def test_n0f8_inputs_equal_their_float32_values_bitwise(pkg, shape, mode):
-    """An N0f8 byte r stands for the correctly rounded Float32 r/255 (FixedPointNumbers).
-    The kernels convert bytes in the loader and then run the same arithmetic as on Float32
-    inputs, so N0f8 images must give bitwise the results of the Float32 images holding those
-    values, on the tile, fused and streaming (above 4 Mi elements) paths.  Every byte value
-    occurs in the images, so a conversion that is off by one ulp for any byte fails here."""
+def test_converted_inputs_equal_their_float32_values_bitwise(pkg, shape, mode, dt):
+    """An N0f8 byte r stands for the correctly rounded Float32 r/255 (FixedPointNumbers), and
+    a Float16 value converts to Float32 exactly.  The kernels convert in the loader and then
+    run the same arithmetic as on Float32 inputs, so converted images must give bitwise the
+    results of the Float32 images holding those values, on the tile, fused and streaming
+    (above 4 Mi elements) paths.  For N0f8 every byte value occurs in the images, so a
+    conversion that is off by one ulp for any byte fails here."""
     syn = _syn(pkg)
-    x8, y8 = syn.host_pair(53, shape, 0.1, dtype=np.uint8)
-    x8.reshape(-1, order="F")[:256] = np.arange(256, dtype=np.uint8)
-    y8.reshape(-1, order="F")[256:512] = np.arange(256, dtype=np.uint8)
-    x32 = np.asfortranarray((x8.astype(np.float64) / 255).astype(np.float32))   # correctly rounded
-    y32 = np.asfortranarray((y8.astype(np.float64) / 255).astype(np.float32))
-    v8, g8 = _run(pkg, x8, y8, mode=mode)
+    if dt == "n0f8":
+        x, y = syn.host_pair(53, shape, 0.1, dtype=np.uint8)
+        x.reshape(-1, order="F")[:256] = np.arange(256, dtype=np.uint8)
+        y.reshape(-1, order="F")[256:512] = np.arange(256, dtype=np.uint8)
+        x32 = np.asfortranarray((x.astype(np.float64) / 255).astype(np.float32))   # correctly rounded
+        y32 = np.asfortranarray((y.astype(np.float64) / 255).astype(np.float32))
+    else:
+        xf, yf = syn.host_pair(53, shape, 0.1)
+        x, y = np.asfortranarray(xf.astype(np.float16)), np.asfortranarray(yf.astype(np.float16))
+        x32, y32 = np.asfortranarray(x.astype(np.float32)), np.asfortranarray(y.astype(np.float32))
+    vc, gc = _run(pkg, x, y, mode=mode)
     v32, g32 = _run(pkg, x32, y32, mode=mode)
-    np.testing.assert_array_equal(v8, v32)
+    np.testing.assert_array_equal(vc, v32)
     if mode == "both":
-        np.testing.assert_array_equal(g8, g32)
+        np.testing.assert_array_equal(gc, g32)
 
 
 def test_float16_gradient_output(pkg, orc):
