@@ -158,6 +158,30 @@ def cpu_batch32_dssim_grad_ms(nthreads, reps=2):
     return best
 
 
+def parity_sample(pkg, x, y, ssims, grad, first_image, seed):
+    """Checks the benchmark batch itself, after the timed region: the first and last image
+    of this rank's shard plus four seeded picks, each against the oracle in single and in
+    double precision.  Returns the largest |delta (D)SSIM| and the largest relative-L2
+    gradient error over the sampled images and both oracle modes."""
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle
+    n = int(ssims.numel())
+    rng = np.random.default_rng(seed)
+    picks = sorted({0, n - 1} | {int(i) for i in rng.choice(n, size=min(4, n), replace=False)})
+    max_ds, max_rel = 0.0, 0.0
+    vals = ssims.double().cpu().numpy()
+    for i in picks:
+        xi, yi = pkg.jl_to_numpy(x[..., i:i + 1]), pkg.jl_to_numpy(y[..., i:i + 1])
+        gi = pkg.jl_to_numpy(grad[..., i:i + 1]).astype(np.float64)
+        for prec in ("f32", "f64"):
+            rv, rg = oracle.ssim(xi, yi, precision=prec)
+            max_ds = max(max_ds, abs(float(vals[i]) - float(rv[0])))
+            max_rel = max(max_rel, float(np.linalg.norm(gi - rg) / max(np.linalg.norm(rg), 1e-30)))
+    return {"images": [first_image + i for i in picks], "max_abs_ssim_err": max_ds,
+            "max_rel_l2_grad_err": max_rel, "oracle": "f32 and f64 modes",
+            "tolerance": {"ssim_abs": 1e-5, "grad_rel_l2": 1e-4}}
+
+
 class CpuSample:
     """A sample of the workload on the host (seeded, same distributions) and the
     oracle (the reference algorithm in single precision, C with pthreads)."""
@@ -284,6 +308,18 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     elapsed, kern = float(t[0]), float(t[1])
 
+    # ---- parity of the timed batch itself (outside the timed region), max over ranks
+    parity = None
+    if not args.no_parity:
+        pr = parity_sample(pkg, x, y, ssims, grad, lo, seed=77 + rank)
+        pt = torch.tensor([pr["max_abs_ssim_err"], pr["max_rel_l2_grad_err"]], dtype=torch.float64, device=dev)
+        if world > 1:
+            dist.all_reduce(pt, op=dist.ReduceOp.MAX)
+        parity = {"max_abs_ssim_err": float(pt[0]), "max_rel_l2_grad_err": float(pt[1]),
+                  "images_per_rank": len(pr["images"]), "rank0_images": pr["images"],
+                  "oracle": pr["oracle"], "tolerance": pr["tolerance"],
+                  "ok": bool(float(pt[0]) <= 1e-5 and float(pt[1]) <= 1e-4)}
+
     # ---- end to end: host buffers through the public API, copies inside the timed region
     e2e = None
     if not args.no_e2e:
@@ -381,6 +417,7 @@ def run_ours(args):
                      "alg_bytes_per_launch": alg_bytes},
         "fp32_pipe": fp32_pipe(kern, n_local, clocks, sms),
         "cpu_baseline": cpu,
+        "parity": parity,
         "e2e": e2e,
         "gpu_launches": args.steps,
         "clocks": clocks,
@@ -477,6 +514,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--no-extras", action="store_true")
+    ap.add_argument("--no-parity", action="store_true")
     ap.add_argument("--profile-case", choices=["fused", "fwd", "fused_u8", "fused_f16", "fused_f64", "fhd1", "fhd3"],
                     default=None,
                     help="only run one kernel on a small case (a size for ncu captures): "
