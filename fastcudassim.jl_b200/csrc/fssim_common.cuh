@@ -228,6 +228,17 @@ __device__ __forceinline__ void static_for(F&& f)
         static_for<B + 1, E>(f);
     }
 }
+// Named barrier `id` over `nthreads` threads (bar.sync with an explicit count).  The
+// two warp groups of the pipelined kernels reach their per-slot barrier from different
+// code; a named barrier with a thread count is defined for that (every warp arrives as
+// a whole), where __syncthreads() is only defined when all threads reach the same call.
+// Barrier 0 stays with __syncthreads() in the block-wide code.
+__device__ __forceinline__ void named_barrier_sync(int id, int nthreads)
+{
+    asm volatile("bar.sync %0, %1;\n" ::"r"(id), "r"(nthreads) : "memory");
+}
+constexpr int BAR_SLOT = 1;   // the per-slot hand-off barrier of the two-group kernels
+
 __device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
 template <int N>
 __device__ __forceinline__ void cp_async_wait()
@@ -270,7 +281,10 @@ __device__ __forceinline__ void finish_image(const Params& p, int n, int local_c
         red[NT / 32] = (ok && prev == static_cast<unsigned>(p.cpi - 1)) ? 1.0 : 0.0;
     }
     __syncthreads();
-    if (red[NT / 32] != 0.0) {   // uniform over the CTA; no early return, so loops may call this
+    // The condition is one shared-memory value read after the barrier, so it is the same
+    // for every thread of the CTA: the barriers inside the branch are block-uniform.
+    // No early return, so loops may call this.
+    if (red[NT / 32] != 0.0) {
         __threadfence();
         double v = 0.0;
         for (int i = threadIdx.x; i < p.cpi; i += NT) {

@@ -365,7 +365,7 @@ __global__ void __launch_bounds__(2 * NT, 512 / (2 * NT)) fwd_pipe_kernel(const 
             load_raw(0);
             store_raw(stage);
         }
-        __syncthreads();
+        named_barrier_sync(BAR_SLOT, 2 * NT);
 #pragma unroll 1
         for (int t = 0; t < nslot; ++t) {
             if (F32IO) {
@@ -403,7 +403,7 @@ __global__ void __launch_bounds__(2 * NT, 512 / (2 * NT)) fwd_pipe_kernel(const 
             }
             if (F32IO) cp_async_wait<0>();
             else if (t + 1 < ns) store_raw(stage + ((t + 1) & 1) * STG);
-            __syncthreads();
+            named_barrier_sync(BAR_SLOT, 2 * NT);
         }
     } else {
         // ================= group B: F2 + SSIM map =================
@@ -454,9 +454,9 @@ __global__ void __launch_bounds__(2 * NT, 512 / (2 * NT)) fwd_pipe_kernel(const 
             TA[1] = Aprv[S - 1];
             TB[0] = Bprv[S - 2];
             TB[1] = Bprv[S - 1];
-            __syncthreads();
+            named_barrier_sync(BAR_SLOT, 2 * NT);
         };
-        __syncthreads();
+        named_barrier_sync(BAR_SLOT, 2 * NT);
 #pragma unroll 1
         for (int t = 0; t < nslot; t += 2) {
             bslot(t, A0, A1, B0, B1);

@@ -18,8 +18,9 @@ namespace fssim {
 //   group B (threads NT..2NT-1):  F2(t-1) + SSIM map + partials, B2(t-3)
 //
 // Every stage reads only what the other group wrote in the previous slot, so a
-// single __syncthreads() per slot orders everything; the buffers passed between
-// the groups are double-buffered by step parity.
+// single barrier per slot (named barrier BAR_SLOT over both groups) orders
+// everything; the buffers passed between the groups are double-buffered by step
+// parity.
 //
 // Group B keeps, per row, the last 10 columns of the F1 output and of the B1
 // output in registers, as two 8-column blocks used in turn (its loop covers two
@@ -229,7 +230,7 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
             load_stage_raw(0);
             store_stage_raw(stage);
         }
-        __syncthreads();
+        named_barrier_sync(BAR_SLOT, 2 * NT);
 #pragma unroll 1
         for (int t = 0; t < nslot; ++t) {
             const bool next_stage = t + 1 < ns;
@@ -304,7 +305,7 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
                 if (next_stage) store_stage_raw(stage + ((t + 1) & 1) * STG);
                 if (next_xy) store_xy_raw(xyb + ((t + 1) & 1) * XYN);
             }
-            __syncthreads();
+            named_barrier_sync(BAR_SLOT, 2 * NT);
         }
     } else {
         // ================= group B: F2 + map, B2 =================
@@ -432,10 +433,10 @@ __global__ void __launch_bounds__(2 * NT, NT == 64 ? 3 : 2) pipe_kernel(const Pa
                 TP[0] = Pprv[S - 2];
                 TP[1] = Pprv[S - 1];
             }
-            __syncthreads();
+            named_barrier_sync(BAR_SLOT, 2 * NT);
         };
 
-        __syncthreads();
+        named_barrier_sync(BAR_SLOT, 2 * NT);
 #pragma unroll 1
         for (int t = 0; t < nslot; t += 2) {
             bslot(t, A0, A1, B0, B1, Q0, Q1, P0, P1);
