@@ -402,7 +402,7 @@ namespace {
 int fwd_bwd_impl(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs1, int grad_dtype,
                  const void* imgs1, int imgs1_dtype, const void* imgs2, int imgs2_dtype, void* qmp, int64_t c,
                  int64_t h, int64_t w, int64_t n, uint32_t flags, void* workspace, size_t workspace_bytes,
-                 void* stream, const void* grad_scale, int grad_scale_dtype)
+                 void* stream, const void* grad_scale, int grad_scale_dtype, bool clear_counters = false)
 {
     (void)qmp;   // the partial gradients never leave the chip (see fastssim.h)
     const uint32_t known = FSSIM_SKIP_SSIM | FSSIM_SKIP_BACKWARD | FSSIM_USE_DSSIM | FSSIM_DIVIDE_BY_TWO |
@@ -520,6 +520,13 @@ int fwd_bwd_impl(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs
     p.isdt = grad_scale_dtype;
 
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (clear_counters && want_ssim) {
+        // Allocation-free entry point: its shared scratch may hold counters that a call
+        // which failed part-way left set.  Cleared only now, after every check has
+        // passed, so a rejected call never touches the scratch.
+        cudaError_t ce = cudaMemsetAsync(workspace, 0, g.ws_counters, s);
+        if (ce != cudaSuccess) return fail(FSSIM_ERR_CUDA, "cudaMemsetAsync(scratch): %s", cudaGetErrorString(ce));
+    }
     void* args[] = {&p};
     cudaError_t e = cudaLaunchKernel(g.ki.fn, dim3(static_cast<unsigned>(g.grid)), dim3(g.ki.threads), args, g.ki.smem, s);
     if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
@@ -604,17 +611,25 @@ extern "C" int fssim_fwd_bwd_noalloc(void* ssims, int ssims_dtype, int64_t ssims
                     "fssim_fwd_bwd_noalloc: these sizes need %zu bytes of reduction scratch, the built-in "
                     "scratch holds %u; call fssim_fwd_bwd with a caller-provided workspace instead",
                     need, (unsigned)FSSIM_NOALLOC_SCRATCH_BYTES);
+    // The scratch used is the current device's: the stream must belong to that device too
+    // (the legacy and per-thread default streams always do).
+    const uintptr_t sv = reinterpret_cast<uintptr_t>(stream);
+    if (sv > 2) {
+        int cur = 0, sdev = 0;
+        cudaError_t e = cudaGetDevice(&cur);
+        if (e == cudaSuccess) e = cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev);
+        if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "stream device query: %s", cudaGetErrorString(e));
+        if (sdev != cur)
+            return fail(FSSIM_ERR_INVALID_ARGUMENT,
+                        "fssim_fwd_bwd_noalloc: the stream belongs to device %d but device %d is current; "
+                        "make the device of the buffers and the stream current", sdev, cur);
+    }
     void* ws = nullptr;
     st = scratch_address(&ws);
     if (st != FSSIM_OK) return st;
-    if (need > 0) {
-        // The per-image counters must start at zero: a previous call that failed
-        // part-way could have left them set.  The partial sums are written before
-        // they are read and need no clearing.
-        const size_t counter_bytes = ((static_cast<size_t>(n) * sizeof(unsigned) + 255) / 256) * 256;
-        const cudaError_t e = cudaMemsetAsync(ws, 0, counter_bytes, static_cast<cudaStream_t>(stream));
-        if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "cudaMemsetAsync(scratch): %s", cudaGetErrorString(e));
-    }
-    return fssim_fwd_bwd(ssims, ssims_dtype, ssims_len, dL_dimgs1, grad_dtype, imgs1, imgs1_dtype, imgs2,
-                         imgs2_dtype, nullptr, c, h, w, n, flags, ws, FSSIM_NOALLOC_SCRATCH_BYTES, stream);
+    // fwd_bwd_impl clears the scratch counters on `stream` once all its argument checks
+    // have passed, just before the launch.
+    return fwd_bwd_impl(ssims, ssims_dtype, ssims_len, dL_dimgs1, grad_dtype, imgs1, imgs1_dtype, imgs2,
+                        imgs2_dtype, nullptr, c, h, w, n, flags, ws, FSSIM_NOALLOC_SCRATCH_BYTES, stream, nullptr,
+                        0, /*clear_counters=*/true);
 }

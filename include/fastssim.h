@@ -161,10 +161,18 @@ int fssim_fwd_bwd_scaled(void* ssims, int ssims_dtype, int64_t ssims_len,
  * workspace.  Limits and rules:
  *  - sizes whose workspace (fssim_workspace_size) exceeds
  *    FSSIM_NOALLOC_SCRATCH_BYTES are rejected with FSSIM_ERR_WORKSPACE;
- *  - no cudaMalloc, cudaFree or allocating library call is made; the scratch
- *    counters are cleared with cudaMemsetAsync on `stream` before the launch;
+ *  - no cudaMalloc, cudaFree or allocating library call is made; once every
+ *    argument check has passed, the scratch counters are cleared with
+ *    cudaMemsetAsync on `stream` just before the launch (a rejected call leaves
+ *    the scratch untouched);
+ *  - the scratch used is that of the CURRENT device at call time: as for
+ *    fssim_fwd_bwd, the current device must be the device that holds the
+ *    buffers, and `stream` must belong to it (FSSIM_ERR_INVALID_ARGUMENT if it
+ *    does not);
  *  - the first call on a device looks up the scratch address on that device
- *    (cudaGetSymbolAddress); make that first call before any stream capture;
+ *    (cudaGetSymbolAddress) and keeps it for later calls; make that first call
+ *    before any stream capture.  Calls must not continue across a
+ *    cudaDeviceReset of that device (the address is not looked up again);
  *  - every call on a device shares the one scratch array: calls that overlap on
  *    the GPU (different streams, no ordering between them) race and give wrong
  *    (D)SSIM values.  Calls on one stream are ordered and safe.
