@@ -73,6 +73,46 @@ def gather_scores(local: torch.Tensor, n_total: int, group=None, deadline_s: flo
     return torch.cat(parts)
 
 
+class ScoreGather:
+    """A reusable all-gather of per-image scores, for a loop that gathers every step.
+
+    The padded send buffer and the output are allocated once.  When every shard has
+    the same length, the shard is gathered straight into the output (no padding, no
+    concatenation).  ``start`` issues the collective asynchronously and returns its
+    handle; the caller may launch the next step's kernel before waiting on it, as long
+    as that kernel does not overwrite the scores being sent (use two score buffers in
+    turn).  ``finish`` waits (with the optional host deadline of ``gather_scores``) and
+    returns the full length-``n_total`` vector."""
+
+    def __init__(self, n_total: int, dtype, device, group=None):
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        self.group = group
+        self.n_total = n_total
+        self.per = -(-n_total // self.world)
+        self.equal = self.per * self.world == n_total
+        self.out = torch.empty(self.per * self.world, dtype=dtype, device=device)
+        self.buf = None if self.equal else torch.zeros(self.per, dtype=dtype, device=device)
+        if not self.equal:
+            idx = []
+            for r in range(self.world):
+                lo, hi = shard_range(n_total, self.world, r)
+                idx.extend(range(r * self.per, r * self.per + (hi - lo)))
+            self.index = torch.tensor(idx, dtype=torch.long, device=device)
+
+    def start(self, local: torch.Tensor):
+        if self.equal:
+            src = local
+        else:
+            self.buf[: local.numel()].copy_(local)
+            src = self.buf
+        return dist.all_gather_into_tensor(self.out, src, group=self.group, async_op=True)
+
+    def finish(self, work, deadline_s: float | None = None) -> torch.Tensor:
+        _wait(work, deadline_s, "all-gather of per-image scores")
+        return self.out if self.equal else self.out.index_select(0, self.index)
+
+
 def sharded_with_gradient(imgs1_shard, imgs2_shard, n_total: int, dssim: bool = False,
                           divide_by_two_in_dssim: bool = False, ssims_shard=None, grad_shard=None,
                           group=None, deadline_s: float | None = None):

@@ -135,3 +135,48 @@ def test_gather_with_deadline_when_every_rank_joins():
         p.join(timeout=60)
         assert p.exitcode == 0
     assert results[0] == results[1] == [float(i) for i in range(7)]
+
+
+def _score_gather_worker(rank, world, port, n_total, q):
+    from datetime import timedelta
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    import sys
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    sys.path.insert(0, root)
+    import __graft_entry__ as ge
+    pkg = ge.load_package()
+    sh = __import__(pkg.__name__ + ".sharded", fromlist=["x"])
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=timedelta(seconds=30))
+    try:
+        g = sh.ScoreGather(n_total, torch.float32, torch.device("cpu"))
+        lo, hi = sh.shard_range(n_total, world, rank)
+        rounds = []
+        for k in range(2):   # the same gatherer, reused: the second round overwrites the first
+            work = g.start(torch.arange(lo, hi, dtype=torch.float32) + 100.0 * k)
+            rounds.append(g.finish(work, deadline_s=30.0).tolist())
+        q.put((rank, rounds, g.equal))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,n_total", [(2, 8), (3, 7), (2, 5)])
+def test_score_gather_reused_across_steps(world, n_total):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_score_gather_worker, args=(r, world, port, n_total, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = {}
+    for _ in range(world):
+        r, rounds, equal = q.get(timeout=120)
+        results[r] = (rounds, equal)
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    for r in range(world):
+        rounds, equal = results[r]
+        assert equal == (n_total % world == 0)
+        for k in range(2):
+            assert rounds[k] == [float(i) + 100.0 * k for i in range(n_total)]
