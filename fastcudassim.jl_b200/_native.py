@@ -28,9 +28,13 @@ ERR_UNSUPPORTED_DTYPE = 3
 ERR_WORKSPACE = 4
 ERR_MISALIGNED = 5
 ERR_CUDA = 6
+ERR_COMM = 7
+ERR_TIMEOUT = 8
 
 EXPORTED_SYMBOLS = ("fssim_version", "fssim_last_error", "fssim_workspace_size", "fssim_fwd_bwd",
-                    "fssim_fwd_bwd_scaled", "fssim_fwd_bwd_noalloc", "fssim_debug_bounds_status")
+                    "fssim_fwd_bwd_scaled", "fssim_fwd_bwd_noalloc", "fssim_debug_bounds_status",
+                    "fssim_comm_unique_id", "fssim_comm_init", "fssim_comm_destroy", "fssim_sharded_workspace_size",
+                    "fssim_fwd_bwd_sharded", "fssim_comm_wait")
 # Size of the scratch array behind fssim_fwd_bwd_noalloc (FSSIM_NOALLOC_SCRATCH_BYTES).
 NOALLOC_SCRATCH_BYTES = 4 << 20
 
@@ -78,6 +82,20 @@ def load() -> ctypes.CDLL:
     lib.fssim_debug_bounds_status.argtypes = [ctypes.POINTER(ctypes.c_uint), ctypes.POINTER(ctypes.c_ulonglong),
                                               ctypes.c_int]
     lib.fssim_debug_bounds_status.restype = ctypes.c_int
+    lib.fssim_comm_unique_id.argtypes = [ctypes.c_char_p]
+    lib.fssim_comm_unique_id.restype = ctypes.c_int
+    lib.fssim_comm_init.argtypes = [ctypes.POINTER(vp), ctypes.c_int, ctypes.c_int, ctypes.c_char_p, ctypes.c_double]
+    lib.fssim_comm_init.restype = ctypes.c_int
+    lib.fssim_comm_destroy.argtypes = [vp, ctypes.c_int]
+    lib.fssim_comm_destroy.restype = ctypes.c_int
+    lib.fssim_sharded_workspace_size.argtypes = [i64, i64, i64, i64, ctypes.c_int, ctypes.c_int, u32, ctypes.c_int,
+                                                 ctypes.POINTER(sz)]
+    lib.fssim_sharded_workspace_size.restype = ctypes.c_int
+    lib.fssim_fwd_bwd_sharded.argtypes = [vp, ctypes.c_int, i64, vp, ctypes.c_int, vp, ctypes.c_int, vp, ctypes.c_int,
+                                          i64, i64, i64, i64, u32, vp, ctypes.c_int, ctypes.c_int, vp, sz, vp]
+    lib.fssim_fwd_bwd_sharded.restype = ctypes.c_int
+    lib.fssim_comm_wait.argtypes = [vp, vp, ctypes.c_double]
+    lib.fssim_comm_wait.restype = ctypes.c_int
     _lib = lib
     return lib
 
@@ -143,3 +161,54 @@ def debug_bounds_status(reset: bool = True) -> tuple[int, int]:
     site, count = ctypes.c_uint(0), ctypes.c_ulonglong(0)
     check(load().fssim_debug_bounds_status(ctypes.byref(site), ctypes.byref(count), int(reset)))
     return int(site.value), int(count.value)
+
+
+# ---- multi-GPU (one process per GPU, NCCL loaded by the library) ----
+
+class CommTimeout(FastSSIMError):
+    """A collective did not finish within its deadline; the communicator was aborted."""
+
+
+def _check_comm(status: int) -> None:
+    if status == ERR_TIMEOUT:
+        raise CommTimeout(status, last_error()[1])
+    check(status)
+
+
+def comm_unique_id() -> bytes:
+    """``fssim_comm_unique_id``: 128 bytes to send from one rank to the others."""
+    buf = ctypes.create_string_buffer(128)
+    check(load().fssim_comm_unique_id(buf))
+    return buf.raw
+
+
+def comm_init(world: int, rank: int, unique_id: bytes, deadline_s: float = 60.0) -> int:
+    """``fssim_comm_init``: an NCCL communicator handle (raises CommTimeout if a rank never joins)."""
+    comm = ctypes.c_void_p(0)
+    _check_comm(load().fssim_comm_init(ctypes.byref(comm), world, rank, unique_id, deadline_s))
+    return int(comm.value)
+
+
+def comm_destroy(comm: int, abort: bool = False) -> None:
+    check(load().fssim_comm_destroy(comm, int(abort)))
+
+
+def sharded_workspace_size(c: int, h: int, w: int, n_total: int, world: int, rank: int, flags: int,
+                           ssims_dtype: int) -> int:
+    out = ctypes.c_size_t(0)
+    check(load().fssim_sharded_workspace_size(c, h, w, n_total, world, rank, flags, ssims_dtype, ctypes.byref(out)))
+    return int(out.value)
+
+
+def fwd_bwd_sharded(all_ptr: int, ssims_dtype: int, n_total: int, grad_ptr: int, grad_dtype: int,
+                    x_ptr: int, x_dtype: int, y_ptr: int, y_dtype: int, c: int, h: int, w: int, n_local: int,
+                    flags: int, comm: int, world: int, rank: int, ws_ptr: int, ws_bytes: int, stream: int) -> None:
+    """``fssim_fwd_bwd_sharded``: this rank's shard, then the all-gather of the values."""
+    _check_comm(load().fssim_fwd_bwd_sharded(all_ptr or None, ssims_dtype, n_total, grad_ptr or None, grad_dtype,
+                                             x_ptr or None, x_dtype, y_ptr or None, y_dtype, c, h, w, n_local, flags,
+                                             comm or None, world, rank, ws_ptr or None, ws_bytes, stream or None))
+
+
+def comm_wait(comm: int, stream: int, deadline_s: float) -> None:
+    """``fssim_comm_wait``: raises CommTimeout (or FastSSIMError) after aborting the communicator."""
+    _check_comm(load().fssim_comm_wait(comm or None, stream or None, deadline_s))

@@ -13,14 +13,14 @@ import sys
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
-SRC = [os.path.join(HERE, "csrc", "fssim.cu")]
+SRC = [os.path.join(HERE, "csrc", "fssim.cu"), os.path.join(HERE, "csrc", "fssim_dist.cu")]
 DEPS = SRC + sorted(glob.glob(os.path.join(HERE, "csrc", "*.cuh"))) + [os.path.join(ROOT, "include", "fastssim.h")]
 OUT = os.path.join(HERE, "lib", "libfastssim.so")
 # The same sources with every global access bounds-checked (tests only).
 OUT_BOUNDS = os.path.join(HERE, "lib", "libfastssim_bounds.so")
 
 NVCC_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a", "-O3", "-lineinfo", "-std=c++17",
-              "-Xcompiler", "-fPIC", "-shared", "-cudart", "static"]
+              "-Xcompiler", "-fPIC", "-shared", "-cudart", "static", "-ldl"]
 
 
 def nvcc() -> str:

@@ -36,6 +36,18 @@ int ok()
     return FSSIM_OK;
 }
 
+}  // namespace
+
+// Status and message of the calling thread, for the library's other translation unit
+// (fssim_dist.cu); not part of the C ABI.
+__attribute__((visibility("hidden"))) int fssim_host_fail(int status, const char* msg)
+{
+    return fail(status, "%s", msg);
+}
+__attribute__((visibility("hidden"))) int fssim_host_ok() { return ok(); }
+
+namespace {
+
 // Gaussian weights, sigma = 1.5, radius 5, evaluated like src/core.jl:40-46:
 // Float32 exp(-0.5 (i/1.5)^2), normalised by their Float32 sum (left to right).
 struct Weights {

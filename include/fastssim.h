@@ -65,7 +65,10 @@ typedef enum fssim_status {
     FSSIM_ERR_UNSUPPORTED_DTYPE = 3,  /* dtype code not accepted for that argument             */
     FSSIM_ERR_WORKSPACE = 4,          /* workspace missing or smaller than fssim_workspace_size */
     FSSIM_ERR_MISALIGNED = 5,         /* a pointer not aligned to its element size             */
-    FSSIM_ERR_CUDA = 6                /* a CUDA runtime error (message has the details)        */
+    FSSIM_ERR_CUDA = 6,               /* a CUDA runtime error (message has the details)        */
+    FSSIM_ERR_COMM = 7,               /* NCCL missing, or an NCCL call / communicator failed   */
+    FSSIM_ERR_TIMEOUT = 8             /* a collective did not finish within its deadline; the
+                                         communicator has been aborted                          */
 } fssim_status;
 
 /* Library version string, e.g. "fastssim 0.1.0 (abi 1, sm_100a)". */
@@ -185,6 +188,64 @@ int fssim_fwd_bwd_noalloc(void* ssims, int ssims_dtype, int64_t ssims_len,
                           const void* imgs2, int imgs2_dtype,
                           int64_t c, int64_t h, int64_t w, int64_t n,
                           uint32_t flags, void* stream);
+
+/*
+ * Multi-GPU: a batch split over the GPUs of one node, one process per GPU.
+ *
+ * No counterpart in the reference's code (FastCUDASSIM.jl runs one GPU per
+ * call); it rests on the reference's per-image independence (src/core.jl:186,
+ * test/batch_order.jl).  Rank `rank` of `world` owns the contiguous shard of
+ * images [lo, lo + n_local) of the n_total images, where the first
+ * n_total % world ranks hold one image more.  The library loads NCCL
+ * (libnccl.so.2, 2.14 or later) at run time; FSSIM_ERR_COMM when it is absent.
+ */
+
+/* A fresh NCCL unique id (128 bytes) for fssim_comm_init; made on one rank and
+ * sent to the others by the caller. */
+int fssim_comm_unique_id(unsigned char id[128]);
+
+/* An NCCL communicator for `rank` of `world` (ncclComm_t, returned as void*).
+ * Created non-blocking and polled: if not every rank joins within deadline_s
+ * seconds the attempt is aborted and FSSIM_ERR_TIMEOUT returned.  A communicator
+ * made by the caller's own NCCL (NCCL.jl, torch) works as well. */
+int fssim_comm_init(void** comm, int world, int rank, const unsigned char id[128], double deadline_s);
+
+/* Destroys a communicator (abort_it = 0: finalise, then destroy) or aborts it
+ * (abort_it != 0: ncclCommAbort, for a communicator a failed peer has left). */
+int fssim_comm_destroy(void* comm, int abort_it);
+
+/* Workspace bytes of fssim_fwd_bwd_sharded for this rank's shard. */
+int fssim_sharded_workspace_size(int64_t c, int64_t h, int64_t w, int64_t n_total, int world, int rank,
+                                 uint32_t flags, int ssims_dtype, size_t* bytes);
+
+/*
+ * fssim_fwd_bwd_sharded - fssim_fwd_bwd on this rank's shard, then the
+ * all-gather of the per-image values, both enqueued on `stream`.
+ *
+ *  all_ssims  length-n_total output on every rank (device), dtype ssims_dtype;
+ *             NULL with FSSIM_SKIP_SSIM (then nothing is exchanged)
+ *  dL_dimgs1, imgs1, imgs2
+ *             this rank's shard (C, H, W, n_local); the gradient stays local
+ *  comm       ncclComm_t of the group (may be NULL when world == 1)
+ * Equal shards are gathered in place in all_ssims; otherwise through padded
+ * buffers in the workspace (size from fssim_sharded_workspace_size).  The
+ * call returns once the work is enqueued: fssim_comm_wait bounds the wait for
+ * it.  Without FSSIM_SHOULD_ZERO the values are added to all_ssims' previous
+ * contents (src/core.jl:919-922).
+ */
+int fssim_fwd_bwd_sharded(void* all_ssims, int ssims_dtype, int64_t n_total,
+                          void* dL_dimgs1, int grad_dtype,
+                          const void* imgs1, int imgs1_dtype,
+                          const void* imgs2, int imgs2_dtype,
+                          int64_t c, int64_t h, int64_t w, int64_t n_local, uint32_t flags,
+                          void* comm, int world, int rank,
+                          void* workspace, size_t workspace_bytes, void* stream);
+
+/* Waits until `stream`'s work has finished, polling it and the communicator's
+ * asynchronous error.  A communicator error, or a deadline that passes first (a
+ * peer that died, hangs or never joined), aborts the communicator and returns
+ * FSSIM_ERR_COMM or FSSIM_ERR_TIMEOUT; the caller then leaves the group. */
+int fssim_comm_wait(void* comm, void* stream, double deadline_s);
 
 #ifdef __cplusplus
 }

@@ -113,3 +113,19 @@ def test_absurd_sizes_are_refused_before_any_cuda_call(pkg):
     st = lib.fssim_fwd_bwd(None, 0, 1, None, 0, x, 0, x, 0, None, 1, 1 << 20, 1 << 20, 1 << 30,
                            nat.SKIP_SSIM | nat.SKIP_BACKWARD, None, 0, None)
     assert st == nat.ERR_INVALID_ARGUMENT and "out of range" in nat.last_error()[1]
+
+
+def test_sharded_entry_checks_its_shard_before_any_cuda_call(pkg):
+    """fssim_fwd_bwd_sharded rejects a rank outside the group and a shard whose size is not
+    the rank's contiguous share (the first n_total % world ranks hold one image more)."""
+    nat = pkg._native
+    lib = nat.load()
+    args = lambda n_total, n_local, world, rank: (ctypes.c_void_p(256), nat.FLOAT32, n_total, ctypes.c_void_p(512),
+                                                  nat.FLOAT32, ctypes.c_void_p(1024), nat.FLOAT32,
+                                                  ctypes.c_void_p(2048), nat.FLOAT32, 3, 8, 8, n_local, 0,
+                                                  ctypes.c_void_p(64), world, rank, None, 0, None)
+    assert lib.fssim_fwd_bwd_sharded(*args(5, 2, 2, 2)) == nat.ERR_INVALID_ARGUMENT      # rank >= world
+    assert lib.fssim_fwd_bwd_sharded(*args(5, 2, 2, 0)) == nat.ERR_DIMENSION_MISMATCH    # rank 0 holds 3 of 5
+    code, msg = nat.last_error()
+    assert "expected a shard of 3 images, got 2" in msg
+    assert lib.fssim_fwd_bwd_sharded(*args(5, 3, 0, 0)) == nat.ERR_INVALID_ARGUMENT      # empty group
