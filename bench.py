@@ -505,6 +505,22 @@ def run_ours(args):
     return 0
 
 
+def c_abi_call_cost(channels):
+    """The library's own per-call cost from C, without Python (tests/c_client/fssim_call_cost.c,
+    built here with gcc): host time of one full-HD forward call, its device time back to back,
+    and one call plus the read of its value."""
+    import tempfile
+    cuda = os.environ.get("CUDA_HOME", "/usr/local/cuda")
+    lib_dir = os.path.join(ROOT, "fastcudassim.jl_b200", "lib")
+    exe = os.path.join(tempfile.mkdtemp(), "fssim_call_cost")
+    subprocess.run(["gcc", "-O2", "-std=c11", "-o", exe, os.path.join(ROOT, "tests", "c_client", "fssim_call_cost.c"),
+                    "-I", os.path.join(ROOT, "include"), "-I", os.path.join(cuda, "include"), "-L", lib_dir,
+                    "-lfastssim", "-L", os.path.join(cuda, "lib64"), "-lcudart", "-Wl,-rpath," + lib_dir],
+                   check=True, capture_output=True)
+    r = subprocess.run([exe, str(channels), "200"], check=True, capture_output=True, text=True, timeout=120)
+    return json.loads(r.stdout.strip().splitlines()[-1])
+
+
 def side_benchmarks(pkg, dev):
     """Full-HD SSIM latency (3x1080x1920 forward) and the 32x3x256x256 DSSIM + gradient call,
     each timed with CUDA events after an L2 flush (their inputs fit in L2)."""
@@ -544,6 +560,11 @@ def side_benchmarks(pkg, dev):
         out[f"{name}_ssim_ms"] = ms
         out[f"{name}_ssim_api_wall_ms"] = statistics.median(walls)
         out[f"{name}_ssim_hbm_frac"] = nbytes / (ms / 1e3) / 1e9 / measured_peaks()[0]
+    for ch in (1, 3):   # the same calls from C: the library's own cost, without the Python layer
+        try:
+            out[f"fullhd_{ch}ch_c_abi"] = c_abi_call_cost(ch)
+        except Exception as e:  # report, do not fail the benchmark line
+            out[f"fullhd_{ch}ch_c_abi"] = {"error": str(e)[:200]}
     x, y = syn.device_pair((3, 256, 256, 32), None, device=dev)
     d = torch.empty(32, dtype=torch.float32, device=dev)
     g = pkg.jl_empty((3, 256, 256, 32), torch.float32, dev)

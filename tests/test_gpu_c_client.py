@@ -43,3 +43,18 @@ def test_c_client_matches_the_oracle(client, pkg, orc, tmp_path, flags):
     rs, rg = orc.ssim(x, y, flags=flags, precision="f32")
     assert np.max(np.abs(s - rs)) <= 1e-5
     assert np.linalg.norm(g - rg) / np.linalg.norm(rg) <= 1e-4
+
+
+@pytest.mark.parametrize("channels", [1, 3])
+def test_c_abi_call_cost(channels):
+    """The per-call cost program builds and runs: SSIM of two zero images is 1, and one call
+    with the read of its value takes longer on the host than the call alone."""
+    import json
+    import sys
+    sys.path.insert(0, ROOT)
+    import bench
+    r = bench.c_abi_call_cost(channels)
+    assert abs(r["ssim_of_zero_images"] - 1.0) < 1e-6
+    assert 0 < r["enqueue_us"] < r["roundtrip_us"]
+    assert r["device_us"] > 0
+    print(json.dumps(r))
