@@ -110,6 +110,19 @@ class ClockSampler:
 # FP32 FMA-equivalents per element of the fused kernel, counted with ncu
 # (sass__inst_executed_per_opcode: FFMA2/FADD2/FMUL2 count 2, FFMA/FADD/FMUL 1).
 FMA_PER_ELEM = 221
+# The forward pass alone: the 4-moment h- and w-passes (2 x 44), the products and the map.
+FWD_FMA_PER_ELEM = 106
+
+
+def fp32_frac(fma_per_elem, elems, ms, sms):
+    """FP32-pipe fraction of a timed call: FMA-equivalents per second against 128 lanes per SM
+    per clock at the maximum SM clock (the clock the side calls run at, not sampled for them)."""
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            mhz = float(json.load(f)["sm_max_mhz"])
+    except Exception:
+        mhz = 1965.0
+    return fma_per_elem * elems / (ms / 1e3) / (sms * 128 * mhz * 1e6)
 
 
 def fp32_pipe(kern_s, n_local, clocks, sms):
@@ -527,6 +540,7 @@ def side_benchmarks(pkg, dev):
     import torch
     syn = __import__(pkg.__name__ + ".synthetic", fromlist=["x"])
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
     out = {}
 
     def timed(fn, reps=30):
@@ -560,6 +574,7 @@ def side_benchmarks(pkg, dev):
         out[f"{name}_ssim_ms"] = ms
         out[f"{name}_ssim_api_wall_ms"] = statistics.median(walls)
         out[f"{name}_ssim_hbm_frac"] = nbytes / (ms / 1e3) / 1e9 / measured_peaks()[0]
+        out[f"{name}_ssim_fp32_frac"] = fp32_frac(FWD_FMA_PER_ELEM, x.numel(), ms, sms)
     for ch in (1, 3):   # the same calls from C: the library's own cost, without the Python layer
         try:
             out[f"fullhd_{ch}ch_c_abi"] = c_abi_call_cost(ch)
@@ -571,6 +586,7 @@ def side_benchmarks(pkg, dev):
     ms = timed(lambda: pkg.dssim_with_gradient_(d, g, x, y, None, True))
     out["batch32_3x256x256_dssim_grad_ms"] = ms
     out["batch32_3x256x256_dssim_grad_hbm_frac"] = x.numel() * 12 / (ms / 1e3) / 1e9 / measured_peaks()[0]
+    out["batch32_3x256x256_dssim_grad_fp32_frac"] = fp32_frac(FMA_PER_ELEM, x.numel(), ms, sms)
     # config 4: 64 x 3 x 512 x 512 in N0f8 and in Float16, Float32 gradient, converted in-kernel
     for tag, dt, nb in (("u8", torch.uint8, 1), ("f16", torch.float16, 2)):
         x, y = syn.device_pair((3, 512, 512, 64), 0.1, dtype=dt, device=dev)
@@ -579,6 +595,7 @@ def side_benchmarks(pkg, dev):
         ms = timed(lambda: pkg.ssim_with_gradient_(s, g, x, y, None, True), reps=10)
         out[f"batch64_3x512x512_{tag}_ssim_grad_ms"] = ms
         out[f"batch64_3x512x512_{tag}_ssim_grad_hbm_frac"] = x.numel() * (2 * nb + 4) / (ms / 1e3) / 1e9 / measured_peaks()[0]
+        out[f"batch64_3x512x512_{tag}_ssim_grad_fp32_frac"] = fp32_frac(FMA_PER_ELEM, x.numel(), ms, sms)
         del x, y, g
     # Float64 inputs, values and gradient (the double-precision kernel): 16 x 3 x 512 x 512
     x, y = syn.device_pair((3, 512, 512, 16), 0.1, dtype=torch.float64, device=dev)
