@@ -378,6 +378,45 @@ def test_workspace_reuse_from_few_to_many_images(pkg, orc):
         _run(pkg, xb, yb, mode=mode)
 
 
+MANY_CTA_CASES = [
+    ("tiles_fwd", (3, 700, 500, 2), "fwd", np.float32),       # 22 x 10 tiles x 3 channels: 660 per image
+    ("tiles_u8", (3, 400, 600, 3), "fwd", np.uint8),          # converted inputs, 390 tiles per image
+    ("stream_fwd", (3, 1500, 1000, 1), "fwd", np.float32),    # streaming forward, above 4 Mi elements
+    ("fused", (3, 1200, 900, 2), "both", np.float32),         # fused: 14 bands x 3 channels x segments
+]
+
+
+@pytest.mark.parametrize("name,shape,mode,dt", MANY_CTA_CASES, ids=[c[0] for c in MANY_CTA_CASES])
+def test_images_of_many_ctas_leave_the_workspace_zeroed(pkg, orc, name, shape, mode, dt):
+    """Images of hundreds of CTAs (tiles, streaming forward, fused): values against the
+    oracle, bitwise equal on a second call, and every counter and partial sum of the
+    workspace zero again after each call (the next call relies on it)."""
+    core = __import__(pkg.__name__ + ".core", fromlist=["x"])
+    syn = _syn(pkg)
+    x, y = syn.host_pair(61, shape, 0.1, dtype=dt)
+    x, y = np.asfortranarray(x), np.asfortranarray(y)
+    xt, yt = pkg.jl_from_numpy(x), pkg.jl_from_numpy(y)
+    C, H, W, N = shape
+    outs = []
+    for _ in range(2):
+        s = torch.empty(N, dtype=torch.float32, device="cuda")
+        g = pkg.jl_empty(shape, torch.float32) if mode == "both" else None
+        if g is None:
+            pkg.ssim_(s, xt, yt)
+        else:
+            pkg.ssim_with_gradient_(s, g, xt, yt, None, True)
+        torch.cuda.synchronize()
+        for ws in core._workspaces.values():
+            assert int(torch.count_nonzero(ws)) == 0
+        outs.append((s.cpu().numpy().astype(np.float64), None if g is None else pkg.jl_to_numpy(g)))
+    np.testing.assert_array_equal(outs[0][0], outs[1][0])
+    rv, rg = orc.ssim(x, y, flags=0 if mode == "both" else orc.SKIP_BACKWARD, precision="f64")
+    assert np.max(np.abs(outs[0][0] - rv)) <= SSIM_ATOL
+    if mode == "both":
+        np.testing.assert_array_equal(outs[0][1], outs[1][1])
+        assert _rel_l2(outs[0][1], rg) <= GRAD_RTOL_L2
+
+
 def test_gradient_into_the_first_input_buffer(pkg, orc):
     """`ssim_gradient!(imgs1, imgs1, imgs2, nothing)` works in the reference (its backward
     launch reads x only at the pixel it writes).  The fused kernel reads neighbouring rows
