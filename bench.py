@@ -559,6 +559,9 @@ def side_benchmarks(pkg, dev):
                 ts.append(a.elapsed_time(b))
         return statistics.median(ts)
 
+    # the floor of these latencies: a one-element kernel timed the same way (launch and events)
+    one = torch.zeros(1, device=dev)
+    out["event_floor_us"] = timed(lambda: one.add_(1.0)) * 1e3
     for name, shape, noise in (("fullhd_1ch", (1, 1080, 1920), 0.1), ("fullhd_3ch", (3, 1080, 1920), 0.05)):
         x, y = syn.device_pair(shape, noise, device=dev)
         s = torch.empty(1, dtype=torch.float32, device=dev)
