@@ -1,6 +1,8 @@
 // C ABI of libfastssim.so: argument checks, launch configuration and the single
 // launch that replaces _ssim_fwd_bwd!'s device work (FastCUDASSIM.jl v0.2.1,
 // src/core.jl:933-1107).  Declarations and the contract live in include/fastssim.h.
+#include <cuda.h>
+#include <cudaTypedefs.h>
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -124,6 +126,12 @@ KInfo tinfo()
                  fssim::TGeo::TW, fssim::TGeo::NT};
 }
 
+KInfo tile_tma_info()
+{
+    return KInfo{reinterpret_cast<const void*>(&fssim::tile_tma_kernel), fssim::TTGeo::total, fssim::TTGeo::TH,
+                 fssim::TTGeo::TW, fssim::TTGeo::NT};
+}
+
 KInfo tile_info(bool f32io, int iom)
 {
     if (f32io) return tinfo<0>();
@@ -212,8 +220,40 @@ int device_facts(const KInfo& ki, int* sms, int* occ)
     return FSSIM_OK;
 }
 
+// cuTensorMapEncodeTiled from the driver (through the runtime, so the library links no
+// driver library); null where the driver does not provide it.
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder()
+{
+    static const PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* f = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+            q != cudaDriverEntryPointSuccess)
+            f = nullptr;
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(f);
+    }();
+    return fn;
+}
+
+// The TMA view of one one-channel Float32 batch: dimensions (H, W, N), the tile kernel's
+// 44 x 64 box.  The caller has checked that H is a multiple of 4 and the base is 16-byte
+// aligned (the strides and the box start must be multiples of 16 bytes).
+bool encode_tile_map(CUtensorMap* m, const void* base, int64_t h, int64_t w, int64_t n)
+{
+    const PFN_cuTensorMapEncodeTiled_v12000 enc = tensor_map_encoder();
+    if (!enc) return false;
+    const cuuint64_t dims[3] = {static_cast<cuuint64_t>(h), static_cast<cuuint64_t>(w), static_cast<cuuint64_t>(n)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(h) * 4u, static_cast<cuuint64_t>(h * w) * 4u};
+    const cuuint32_t box[3] = {fssim::TTGeo::BR, fssim::TTGeo::IC, 1};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    return enc(m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, const_cast<void*>(base), dims, strides, box, estr,
+               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_128B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 struct Cfg {
     bool fused = false, want_ssim = false;
+    bool tma = false;   // tile kernel with TMA loads (tile_tma_kernel)
     int nt = 0, T = 0, nb = 0, nseg = 0, L = 0;
     int64_t cpi = 0, grid = 0;
     KInfo ki{};
@@ -228,7 +268,8 @@ constexpr int IOM_F64 = 4;   // configure(): compute in double precision
 // {64, 96, 128} (forward only) to minimise padded rows, then the number of
 // width segments that best fills the GPU (whole waves of resident CTAs
 // versus the 10-20 warm-up columns each extra segment costs).
-int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f32io, int iom, Cfg* cfg)
+int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f32io, int iom, Cfg* cfg,
+              bool tma_ok = false)
 {
     Cfg g;
     g.fused = !(flags & FSSIM_SKIP_BACKWARD);
@@ -255,13 +296,16 @@ int configure(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t flags, bool f
         return FSSIM_OK;
     }
     if (!g.fused && use_tiles(c, h, w, n, f32io, iom)) {   // small forward-only call: one TH x TW tile per CTA
-        g.ki = tile_info(f32io, iom);
+        // one-channel Float32 images with a height divisible by 4 load their tiles with TMA
+        // (tile rows shifted by TTGeo::SHIFT, so that every box starts 16-byte aligned)
+        g.tma = tma_ok && f32io && c == 1 && h % 4 == 0;
+        g.ki = g.tma ? tile_tma_info() : tile_info(f32io, iom);
         int sms = 0, occ = 0;
         int st = device_facts(g.ki, &sms, &occ);
         if (st != FSSIM_OK) return st;
         g.nt = fssim::TGeo::TH;
         g.T = fssim::TGeo::TH;
-        g.nb = static_cast<int>(cdiv(h, fssim::TGeo::TH));
+        g.nb = static_cast<int>(g.tma ? cdiv(h + fssim::TTGeo::SHIFT, fssim::TTGeo::TH) : cdiv(h, fssim::TGeo::TH));
         g.nseg = static_cast<int>(cdiv(w, fssim::TGeo::TW));
         g.L = fssim::TGeo::TW;
         g.cpi = c * g.nb * g.nseg;
@@ -399,7 +443,7 @@ int fssim_workspace_size(int64_t c, int64_t h, int64_t w, int64_t n, uint32_t fl
     size_t most = 0;
     for (int v = 0; v <= IOM_F64; ++v) {
         Cfg g;
-        st = configure(c, h, w, n, flags, v == 0, v == 0 ? fssim::IN_ANY : v, &g);
+        st = configure(c, h, w, n, flags, v == 0, v == 0 ? fssim::IN_ANY : v, &g, v == 0);
         if (st != FSSIM_OK) return st;
         most = std::max(most, g.ws_bytes);
     }
@@ -483,8 +527,14 @@ int fwd_bwd_impl(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs
     // Float64 on either input: compute in double (promote_type(T1, T2, Float32), src/core.jl:953-954)
     const bool f64 = imgs1_dtype == FSSIM_FLOAT64 || imgs2_dtype == FSSIM_FLOAT64;
     Cfg g;
-    st = configure(c, h, w, n, flags, f32io && !f64, f64 ? IOM_F64 : iom, &g);
+    const bool tma_ok = aligned(imgs1, 16) && aligned(imgs2, 16);
+    st = configure(c, h, w, n, flags, f32io && !f64, f64 ? IOM_F64 : iom, &g, tma_ok);
     if (st != FSSIM_OK) return st;
+    CUtensorMap tmx, tmy;
+    if (g.tma && !(encode_tile_map(&tmx, imgs1, h, w, n) && encode_tile_map(&tmy, imgs2, h, w, n))) {
+        st = configure(c, h, w, n, flags, f32io && !f64, f64 ? IOM_F64 : iom, &g, false);   // plain tile loads
+        if (st != FSSIM_OK) return st;
+    }
     if (want_ssim) {
         if (!workspace || workspace_bytes < g.ws_bytes)
             return fail(FSSIM_ERR_WORKSPACE, "workspace of %zu bytes required, got %zu", g.ws_bytes,
@@ -539,7 +589,7 @@ int fwd_bwd_impl(void* ssims, int ssims_dtype, int64_t ssims_len, void* dL_dimgs
         cudaError_t ce = cudaMemsetAsync(workspace, 0, g.ws_counters, s);
         if (ce != cudaSuccess) return fail(FSSIM_ERR_CUDA, "cudaMemsetAsync(scratch): %s", cudaGetErrorString(ce));
     }
-    void* args[] = {&p};
+    void* args[] = {&p, &tmx, &tmy};   // the tensor maps only for the TMA tile kernel
     cudaError_t e = cudaLaunchKernel(g.ki.fn, dim3(static_cast<unsigned>(g.grid)), dim3(g.ki.threads), args, g.ki.smem, s);
     if (e != cudaSuccess) return fail(FSSIM_ERR_CUDA, "kernel launch failed: %s", cudaGetErrorString(e));
     return ok();

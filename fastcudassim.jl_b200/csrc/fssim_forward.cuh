@@ -2,6 +2,8 @@
 // (tile_fwd_kernel) and the single-group streaming kernel with 64-bit offsets (band_kernel).
 #pragma once
 
+#include <cuda.h>   // CUtensorMap
+
 #include "fssim_common.cuh"
 
 namespace fssim {
@@ -675,6 +677,196 @@ __global__ void __launch_bounds__(TGeo::NT, 4) tile_fwd_kernel(const Params p)
         finish_image<G::NT>(p, u.n, (u.th * p.nseg + u.tw) * C + u.c, tsum, red);
     }
 #undef FSSIM_K2
+}
+
+// ---------------------------------------------------------------------------
+// Tile kernel with TMA loads: one-channel Float32 images whose height is a
+// multiple of 4.  The same three phases as tile_fwd_kernel, but the input tile
+// arrives as two tensor-memory-access boxes (x and y), issued by one thread and
+// completed on an mbarrier, so the CTA spends no instructions on the loads.
+//
+// A TMA box must start at a 16-byte boundary of the contiguous (height) axis.
+// Tile rows therefore start at 32*th - 3, so that each box starts at image row
+// 32*th - 8, a multiple of 4.  The box is 44 rows by 64 columns and lands in
+// shared memory as [column][row]: its 44-float columns are 11 16-byte chunks, an
+// odd number, so the h-pass reads four rows per 16-byte load without bank
+// conflicts.  Rows and columns outside the image are filled with zeros by the
+// copy itself.  The wait on the mbarrier is bounded; were it ever to run out,
+// the tile's sum becomes NaN, so the image's value shows it.
+// ---------------------------------------------------------------------------
+struct TTGeo {
+    static constexpr int TH = 32, TW = 54;           // output tile: rows (h) x columns (w)
+    static constexpr int NT = 256;
+    static constexpr int SHIFT = 3;                  // tile th covers rows 32*th - 3 .. 32*th + 28
+    static constexpr int BR = 44;                    // box rows: 32*th - 8 .. 32*th + 35
+    static constexpr int IC = TW + 2 * RAD;          // box columns = F1 output columns (64)
+    static constexpr int NG = (TW + V - 1) / V;      // F2 column groups of V outputs per row
+    static constexpr int FS = NG * V + 2 * RAD + 1;  // F1 row stride (float4), odd
+    static constexpr int plane_bytes = IC * BR * 4;  // one input's box
+    static constexpr int f1_bytes = TH * FS * 16;
+    static constexpr int red_bytes = (NT / 32 + 2) * 8;
+    static constexpr int off_x = 0, off_y = plane_bytes, off_f1 = 2 * plane_bytes;
+    static constexpr int off_red = off_f1 + f1_bytes, off_bar = off_red + red_bytes;
+    static constexpr int total = off_bar + 8;
+    static constexpr unsigned tx_bytes = 2u * plane_bytes;
+    static_assert(BR % 4 == 0 && (BR / 4) % 2 == 1, "box columns: an odd number of whole 16-byte chunks");
+    static_assert((SHIFT + RAD) % 4 == 0 && TH % 4 == 0, "every box starts at a multiple of 4 rows");
+    static_assert(TH + 2 * RAD <= BR, "the box covers the tile's rows and their halo");
+    static_assert(V * (TH / V - 1) + 4 * ((V + 2 * RAD + 3) / 4) <= BR, "the h-pass reads whole chunks inside the box");
+    static_assert(IC * (TH / V) == NT && TH * NG <= NT, "one F1 item and at most one F2 item per thread");
+    static_assert(FS % 2 == 1 && plane_bytes % 128 == 0 && off_bar % 8 == 0, "strides and alignment");
+};
+
+__device__ __forceinline__ void tma_load_3d(unsigned dst, const CUtensorMap* tm, int x, int y, int z, unsigned bar)
+{
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], [%5];\n"
+        ::"r"(dst), "l"(reinterpret_cast<uint64_t>(tm)), "r"(x), "r"(y), "r"(z), "r"(bar)
+        : "memory");
+}
+
+// Waits for phase `phase` of the mbarrier at `bar`; false if it did not complete
+// within the bound (each try_wait may itself suspend the thread for a while).
+__device__ __forceinline__ bool mbar_wait_bounded(unsigned bar, unsigned phase)
+{
+    for (int i = 0; i < (1 << 20); ++i) {
+        unsigned done;
+        asm volatile(
+            "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+            : "=r"(done)
+            : "r"(bar), "r"(phase)
+            : "memory");
+        if (done) return true;
+    }
+    return false;
+}
+
+__global__ void __launch_bounds__(TTGeo::NT, 4)
+    tile_tma_kernel(const Params p, const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmy)
+{
+    using G = TTGeo;
+    constexpr int TH = G::TH, TW = G::TW, IC = G::IC, BR = G::BR, FS = G::FS;
+    extern __shared__ __align__(128) unsigned char smem_tma[];
+    float* sx = reinterpret_cast<float*>(smem_tma + G::off_x);       // [IC][BR]
+    float* sy = reinterpret_cast<float*>(smem_tma + G::off_y);
+    float4* f1 = reinterpret_cast<float4*>(smem_tma + G::off_f1);    // [TH][FS]
+    double* red = reinterpret_cast<double*>(smem_tma + G::off_red);
+    const unsigned bar = smem_addr(smem_tma + G::off_bar);
+
+    const int tid = threadIdx.x;
+    const int H = p.H, W = p.W;
+    // block -> (tile column, tile row, image); one channel; 32-bit divisions (grid < 2^31)
+    const uint32_t b0 = blockIdx.x, q1b = b0 / static_cast<uint32_t>(p.nseg), q2b = q1b / static_cast<uint32_t>(p.nb);
+    const int tw = static_cast<int>(b0 - q1b * static_cast<uint32_t>(p.nseg));
+    const int th = static_cast<int>(q1b - q2b * static_cast<uint32_t>(p.nb));
+    const int n = static_cast<int>(q2b);
+
+    if (tid == 0) {
+        asm volatile("mbarrier.init.shared::cta.b64 [%0], 1;\n" ::"r"(bar) : "memory");
+        asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+    }
+    // F1 columns past IC feed only outputs outside the tile: keep them finite
+    for (int e = tid; e < TH * (FS - IC); e += G::NT)
+        f1[(e / (FS - IC)) * FS + IC + e % (FS - IC)] = make_float4(0.f, 0.f, 0.f, 0.f);
+    __syncthreads();
+    if (tid == 0) {
+        asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(bar), "r"(G::tx_bytes)
+                     : "memory");
+        const int r0 = th * TH - G::SHIFT - RAD;   // 32*th - 8: 16-byte aligned
+        const int c0 = tw * TW - RAD;
+        tma_load_3d(smem_addr(sx), &tmx, r0, c0, n, bar);
+        tma_load_3d(smem_addr(sy), &tmy, r0, c0, n, bar);
+    }
+    float2 KP[RAD + 1];
+#pragma unroll
+    for (int i = 0; i <= RAD; ++i) KP[i] = make_float2(p.kh[i], p.kh[i]);
+#define FSSIM_K2(tap) KP[(tap) <= RAD ? (tap) : 2 * RAD - (tap)]
+    const bool landed = mbar_wait_bounded(bar, 0u);
+
+    // ---- F1: rows V*q1 .. V*q1+V-1 of column q (box rows V*q1 .. V*q1+V+2R-1)
+    {
+        const int q = tid % IC, q1 = tid / IC;
+        const float4* cx = reinterpret_cast<const float4*>(sx + q * BR + V * q1);
+        const float4* cy = reinterpret_cast<const float4*>(sy + q * BR + V * q1);
+        float2 aA[V], aB[V];
+#pragma unroll
+        for (int o = 0; o < V; ++o) {
+            aA[o] = make_float2(0.f, 0.f);
+            aB[o] = make_float2(0.f, 0.f);
+        }
+#pragma unroll
+        for (int ch = 0; ch < (V + 2 * RAD + 3) / 4; ++ch) {
+            const float4 x4 = cx[ch], y4 = cy[ch];
+            const float xr[4] = {x4.x, x4.y, x4.z, x4.w}, yr[4] = {y4.x, y4.y, y4.z, y4.w};
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int i = 4 * ch + j;
+                if (i < V + 2 * RAD) {
+                    const float2 xy = make_float2(xr[j], yr[j]);
+                    const float2 sq = __fmul2_rn(xy, xy);
+                    const float2 sb = make_float2(sq.x + sq.y, xy.x * xy.y);   // (x^2+y^2, xy)
+#pragma unroll
+                    for (int o = 0; o < V; ++o) {
+                        const int tap = i - o;
+                        if (tap >= 0 && tap < TAPS) {
+                            aA[o] = __ffma2_rn(xy, FSSIM_K2(tap), aA[o]);
+                            aB[o] = __ffma2_rn(sb, FSSIM_K2(tap), aB[o]);
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int o = 0; o < V; ++o)
+            f1[(V * q1 + o) * FS + q] = make_float4(aA[o].x, aA[o].y, aB[o].x, aB[o].y);
+    }
+    __syncthreads();
+
+    // ---- F2 + map: row r, output columns V*g .. V*g+V-1 of the tile
+    double tsum = 0.0;
+    {
+        const int r = tid % TH, g = tid / TH;
+        if (g < G::NG) {
+            float2 a[V], b[V];
+#pragma unroll
+            for (int o = 0; o < V; ++o) {
+                a[o] = make_float2(0.f, 0.f);
+                b[o] = make_float2(0.f, 0.f);
+            }
+#pragma unroll
+            for (int m = 0; m < V + 2 * RAD; ++m) {
+                const float4 v = f1[r * FS + V * g + m];
+                const float2 va = make_float2(v.x, v.y), vb = make_float2(v.z, v.w);
+#pragma unroll
+                for (int o = 0; o < V; ++o) {
+                    const int tap = m - o;
+                    if (tap >= 0 && tap < TAPS) {
+                        a[o] = __ffma2_rn(va, FSSIM_K2(tap), a[o]);
+                        b[o] = __ffma2_rn(vb, FSSIM_K2(tap), b[o]);
+                    }
+                }
+            }
+            const int hr = th * TH - G::SHIFT + r, w0 = tw * TW;
+            float ssum = 0.f;
+#pragma unroll
+            for (int o = 0; o < V; ++o) {
+                const float mx = a[o].x, my = a[o].y, qs = b[o].x, pxy = b[o].y;
+                const float2 sq = __fmul2_rn(a[o], a[o]);
+                const float mxy = mx * my;
+                const float sumsq = sq.x + sq.y;
+                const float z = sumsq + p.C1;
+                const float tt = (qs - sumsq) + p.C2;
+                const float ax = fmaf(2.f, mxy, p.C1);
+                const float by = fmaf(2.f, pxy - mxy, p.C2);
+                const float sv = (ax * by) * rcp_approx(z * tt);
+                const int col = V * g + o;
+                if (static_cast<unsigned>(hr) < static_cast<unsigned>(H) && col < TW && w0 + col < W) ssum += sv;
+            }
+            tsum = landed ? static_cast<double>(ssum) : __longlong_as_double(0x7ff8000000000000ll);
+        }
+    }
+#undef FSSIM_K2
+    finish_image<G::NT>(p, n, th * p.nseg + tw, tsum, red);
 }
 
 }  // namespace fssim

@@ -417,6 +417,38 @@ def test_images_of_many_ctas_leave_the_workspace_zeroed(pkg, orc, name, shape, m
         assert _rel_l2(outs[0][1], rg) <= GRAD_RTOL_L2
 
 
+TMA_TILE_SHAPES = [(1, 1080, 1920, 1), (1, 4, 5, 3), (1, 8, 64, 2), (1, 28, 54, 1), (1, 32, 55, 2),
+                   (1, 100, 300, 4), (1, 512, 512, 3)]
+
+
+@pytest.mark.parametrize("shape", TMA_TILE_SHAPES, ids=["x".join(map(str, s)) for s in TMA_TILE_SHAPES])
+def test_tma_tiles_vs_oracle(pkg, orc, shape):
+    """One-channel Float32 forward calls with a height divisible by 4 load their tiles with
+    TMA (tile rows shifted by 3, boxes zero-filled outside the image).  Against the oracle,
+    bitwise equal on a second call; a view one element off 16-byte alignment takes the plain
+    loads and must agree within the tolerance."""
+    syn = _syn(pkg)
+    x, y = syn.host_pair(67, shape, 0.1)
+    v, _ = _run(pkg, x, y, mode="fwd")
+    v2, _ = _run(pkg, x, y, mode="fwd")
+    rv, _ = orc.ssim(x, y, flags=orc.SKIP_BACKWARD, precision="f64")
+    assert np.max(np.abs(v - rv)) <= SSIM_ATOL, (v, rv)
+    np.testing.assert_array_equal(v, v2)
+    # the same images, one element into a larger buffer: not 16-byte aligned
+    C, H, W, N = shape
+    n_el = C * H * W * N
+    bx = torch.empty(n_el + 1, dtype=torch.float32, device="cuda")
+    by = torch.empty(n_el + 1, dtype=torch.float32, device="cuda")
+    bx[1:] = torch.from_numpy(np.asfortranarray(x).reshape(-1, order="F")).cuda()
+    by[1:] = torch.from_numpy(np.asfortranarray(y).reshape(-1, order="F")).cuda()
+    xv = bx[1:].as_strided((C, H, W, N), (1, C, C * H, C * H * W))
+    yv = by[1:].as_strided((C, H, W, N), (1, C, C * H, C * H * W))
+    out = torch.empty(N, dtype=torch.float32, device="cuda")
+    pkg.ssim_(out, xv, yv)
+    torch.cuda.synchronize()
+    assert np.max(np.abs(out.cpu().numpy().astype(np.float64) - rv)) <= SSIM_ATOL
+
+
 def test_gradient_into_the_first_input_buffer(pkg, orc):
     """`ssim_gradient!(imgs1, imgs1, imgs2, nothing)` works in the reference (its backward
     launch reads x only at the pixel it writes).  The fused kernel reads neighbouring rows
