@@ -4,7 +4,7 @@ There every global access checks its element index against the array first and
 records a failure instead of making the access; compute-sanitizer is not
 available, so this is the memory check.  A child process loads the library and
 runs tiny, odd and batch shapes through each kernel (fused SSIM + gradient,
-gradient with a per-image factor, forward tiles and streaming, converted and
+gradient with a per-image factor, forward tiles (plain and TMA loads) and streaming, converted and
 Float64 inputs, the no-alloc entry point): no access may be out of range, and
 the values must equal the regular build's.
 """
@@ -34,7 +34,8 @@ if CHECKED:
     nat.debug_bounds_status(reset=True)
 out = {}
 cases = [((1, 1, 1, 2), "f32"), ((1, 37, 5, 1), "f32"), ((3, 1023, 767, 1), "f32"), ((2, 57, 33, 3), "u8"),
-         ((4, 40, 129, 2), "f16"), ((3, 53, 41, 2), "f64"), ((3, 1100, 1400, 1), "f32"), ((5, 31, 20, 1), "f32")]
+         ((4, 40, 129, 2), "f16"), ((3, 53, 41, 2), "f64"), ((3, 1100, 1400, 1), "f32"), ((5, 31, 20, 1), "f32"),
+         ((1, 64, 70, 2), "f32")]   # one channel, height divisible by 4: the TMA tile loads
 for shape, dt in cases:
     x, y = syn.host_pair(3, shape, 0.1, dtype=np.uint8 if dt == "u8" else np.float64)
     if dt != "u8":
