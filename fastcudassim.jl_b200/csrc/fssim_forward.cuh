@@ -821,6 +821,8 @@ __global__ void __launch_bounds__(TTGeo::NT, 4)
             f1[(V * q1 + o) * FS + q] = make_float4(aA[o].x, aA[o].y, aB[o].x, aB[o].y);
     }
     __syncthreads();
+    // every thread is past the wait: the mbarrier's word goes back to plain shared memory
+    if (tid == 0) asm volatile("mbarrier.inval.shared::cta.b64 [%0];\n" ::"r"(bar) : "memory");
 
     // ---- F2 + map: row r, output columns V*g .. V*g+V-1 of the tile
     double tsum = 0.0;
