@@ -268,10 +268,11 @@ def test_float64_gradient_output_from_float32_inputs(pkg, orc):
     assert _rel_l2(pkg.jl_to_numpy(g), rg) <= GRAD_RTOL_L2
 
 
-@pytest.mark.parametrize("shape", [(3, 1100, 1400, 1), (1, 600, 800, 10)], ids=["3x1100x1400", "10x1x600x800"])
+@pytest.mark.parametrize("shape", [(3, 1100, 1400, 1), (1, 600, 800, 10), (3, 256, 256, 16)],
+                         ids=["3x1100x1400", "10x1x600x800", "16x3x256x256"])
 def test_forward_streaming_kernel_vs_oracle(pkg, orc, shape):
-    """Float32 forward calls above 4 Mi elements take the streaming kernel (smaller ones and
-    converted inputs run as tiles): the same tolerance against the float64 oracle."""
+    """Float32 forward calls above 4 Mi elements (several channels: from 3 Mi) take the streaming
+    kernel (smaller ones run as tiles): the same tolerance against the float64 oracle."""
     x, y = _syn(pkg).host_pair(29, shape, 0.1)
     v, _ = _run(pkg, x, y, mode="fwd")
     rv, _ = orc.ssim(x, y, flags=orc.SKIP_BACKWARD, precision="f64")
