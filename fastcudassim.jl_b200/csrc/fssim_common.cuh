@@ -28,7 +28,8 @@
 // gradient and one double per CTA ever touches global memory.
 //
 // Kernels: pipe_kernel (SSIM + gradient, two warp groups); forward only:
-// fwd_pipe_kernel (its forward half, calls above 4 Mi elements), tile_fwd_kernel
+// fwd_pipe_kernel (its forward half, calls above 4 Mi elements, Float32 calls of several
+// channels from 3 Mi), tile_fwd_kernel / tile_tma_kernel
 // (smaller calls, mixed input dtypes) and band_kernel (single group, 64-bit
 // offsets: Float32 images of 2^31 elements or more); f64_kernel (any call with
 // a Float64 input, in double precision).
